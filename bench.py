@@ -1,0 +1,460 @@
+#!/usr/bin/env python3
+"""Benchmark of the TriAttention eviction step (score -> select -> compact).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME]
+                    [--impl ours|reference] [--scaling weak|strong]
+
+One step = one tria_evict call over the whole cache (every (layer, kv-head)
+of the workload): score every row, select the rows to keep, compact K/V and
+positions into the ping-pong buffer.  Inputs are resident in HBM and larger
+than L2 (no flush needed).  Prints one JSON line on rank 0.
+
+Under torchrun (N > 1) every rank runs its own shard:
+  --scaling weak   (default) each rank evicts a full cache of the workload
+                   (per-GPU work fixed; e.g. one sequence per GPU);
+  --scaling strong the workload's kv heads are split across the ranks (total
+                   work fixed).
+The step is timed on the device with CUDA events and reported as the max over
+ranks.  `--impl reference` times the reference's CPU implementation
+(oracle/_ref = the reference's triattention.c, plus the oracle's select and
+compact) on the host cores with all threads, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import tempfile
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "triattention-ggml_b200"))
+sys.path.insert(0, os.path.join(REPO, "oracle"))
+
+import numpy as np  # noqa: E402
+
+import workloads  # noqa: E402
+
+METRIC = "KV rows scored+evicted+compacted per sec"
+UNIT = "rows/s"
+FALLBACK_HBM_GBS = 6650.0
+
+CONFIGS = {
+    # Qwen3-8B geometry, the north-star step
+    "qwen3-8b-f16-32k": dict(L=36, H=32, KV=8, hd=128, n=32768, type=workloads.TYPE_F16,
+                             budget_pct=12, ramp=100, theta=1e6),
+    # 27B-class geometry (64 layers, gqa 5)
+    "27b-f16-64k": dict(L=64, H=40, KV=8, hd=128, n=65536, type=workloads.TYPE_F16,
+                        budget_pct=12, ramp=100, theta=1e6),
+    # q8_0 cache, 65536 rows, one eviction at a 512-row budget (last ramp stage)
+    "qwen3-8b-q8_0-64k": dict(L=36, H=32, KV=8, hd=128, n=65536, type=workloads.TYPE_Q8_0,
+                              budget=512, ramp=100, theta=1e6),
+}
+DEFAULT_CONFIG = "qwen3-8b-f16-32k"
+
+
+def describe(cfg_name, c, budget):
+    t = "f16" if c["type"] == workloads.TYPE_F16 else "q8_0"
+    return (f"{cfg_name}: {c['L']} layers x {c['KV']} kv heads x {c['n']} rows, head_dim {c['hd']}, "
+            f"gqa {c['H'] // c['KV']}, {t} K/V, budget {budget} rows per (layer, kv-head), ramp {c['ramp']}%")
+
+
+def budget_rows(c):
+    return int(c["n"] * c["budget_pct"] / 100) if "budget_pct" in c else int(c["budget"])
+
+
+def step_bytes(c, units, keep):
+    """Algorithmic bytes per step: n*Rb (K read) + 4*B*Rb (kept K, V read + write)
+    + 4*n (positions read) + 8*B (positions moved), summed over units."""
+    rb = workloads.row_bytes(c["type"], c["hd"])
+    n = c["n"]
+    return units * (n * rb + 4 * keep * rb + 4 * n + 8 * keep)
+
+
+def score_kernel_bytes(c, units):
+    rb = workloads.row_bytes(c["type"], c["hd"])
+    return units * c["n"] * (rb + 4)
+
+
+def measured_peak():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(kernel, workload):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, or None."""
+    p = os.path.join(REPO, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)[workload][kernel]["dram_bytes_per_launch"]
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML (read-only) in a thread."""
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting"}
+
+    def __init__(self, torch_device_index, period=0.02):
+        self.ok = False
+        self.samples = []
+        self.max_mhz = None
+        try:
+            import pynvml as N
+            import torch
+            N.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(torch_device_index).uuid)
+            self.h = N.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            self.N = N
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # pragma: no cover - depends on the box
+            self.err = repr(e)
+        self.period = period
+        self._stop = threading.Event()
+
+    def _run(self):
+        N = self.N
+        while not self._stop.is_set():
+            try:
+                mhz = N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)
+                rs = N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((mhz, rs))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "note": getattr(self, "err", "no samples")}
+        mhz = [m for m, _ in self.samples]
+        reasons = set()
+        for _, rs in self.samples:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        return {"sm_mhz": float(statistics.median(mhz)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------- CPU baseline
+
+def cpu_step_rate(c, stats_path, n_units, seed=0, threads=None, data=None):
+    """Run the reference CPU step (reference tria_score_kv_head + oracle select and
+    compact, pthreads over units) on n_units units of the workload.
+    Returns (rows/s, seconds, threads, kind)."""
+    import oracle_py
+    orc = oracle_py.Oracle()
+    if oracle_py.RefLib.available():
+        ref = oracle_py.RefLib()
+        load, free, fn, kind = ref.load, ref.free, ref.score_fn_ptr, "reference"
+    else:
+        load, free, fn, kind = orc.load, orc.free, orc.score_fn_ptr, "port"
+    threads = threads or len(os.sched_getaffinity(0))
+    hd, KV, n = c["hd"], c["KV"], c["n"]
+    rb = workloads.row_bytes(c["type"], hd)
+    n_layer = max(1, (n_units + KV - 1) // KV)
+    if data is None:
+        if c["type"] == workloads.TYPE_F16:
+            K = workloads.f16_cache(n_layer, n, KV, hd, seed=seed)
+            V = workloads.f16_cache(n_layer, n, KV, hd, seed=seed + 1)
+        else:
+            K = workloads.q8_0_cache(n_layer, n, KV, hd, seed=seed)
+            V = workloads.q8_0_cache(n_layer, n, KV, hd, seed=seed + 1)
+    else:
+        K, V = data
+    Ko, Vo = np.zeros_like(K), np.zeros_like(V)
+    pos = np.arange(n, dtype=np.int32)
+    pos_o = np.zeros((n_units, n), np.int32)
+    keep = workloads.layer_keep(n, budget_rows(c), c["ramp"])
+    st = load(stats_path)
+    units = []
+    for u in range(n_units):
+        l, h = divmod(u, KV)
+        units.append(oracle_py.OracleUnit(l, h, n, keep, K[l, :, h * rb:].ctypes.data,
+                                          V[l, :, h * rb:].ctypes.data, Ko[l, :, h * rb:].ctypes.data,
+                                          Vo[l, :, h * rb:].ctypes.data, pos.ctypes.data,
+                                          pos_o[u].ctypes.data, 0))
+    t0 = time.perf_counter()
+    rc = orc.cpu_step(fn, st, c["type"], hd, KV * rb, units, n, 0, 0, threads)
+    dt = time.perf_counter() - t0
+    free(st)
+    assert rc == 0
+    return n_units * n / dt, dt, threads, kind
+
+
+def write_stats(c, td):
+    path = os.path.join(td, "bench.tria")
+    workloads.write_tria(path, c["L"], c["H"], c["KV"], c["hd"], rope_theta=c["theta"], seed=0)
+    return path
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path on the host cores, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    c = CONFIGS[args.config]
+    threads = len(os.sched_getaffinity(0))
+    with tempfile.TemporaryDirectory() as td:
+        path = write_stats(c, td)
+        # size one step to ~4 s of wall time: one probe unit per thread first
+        _, dt1, _, _ = cpu_step_rate(c, path, min(threads, c["L"] * c["KV"]), seed=1, threads=threads)
+        per_unit_thread = dt1 / max(1, -(-min(threads, c["L"] * c["KV"]) // threads))
+        units = int(max(1, min(c["L"] * c["KV"], threads * max(1, round(4.0 / per_unit_thread)))))
+        rates = []
+        kind = "reference"
+        for i in range(args.warmup + args.steps):
+            r, dt, th, kind = cpu_step_rate(c, path, units, seed=2 + i, threads=threads)
+            if i >= args.warmup:
+                rates.append((r, dt))
+    value = statistics.median(r for r, _ in rates)
+    ms = statistics.median(dt for _, dt in rates) * 1e3
+    sample = f"{units} of {c['L'] * c['KV']} (layer, kv-head) units x {c['n']} rows per step"
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded numpy, same distributions)",
+            "config": {"workload": describe(args.config, c, budget_rows(c))},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import devcache
+    import tria_b200
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    c = CONFIGS[args.config]
+    budget = budget_rows(c)
+
+    # shard
+    if args.scaling == "strong" and world > 1:
+        assert c["KV"] % world == 0, "strong scaling splits the kv heads evenly"
+        n_head_kv, head0 = c["KV"] // world, rank * (c["KV"] // world)
+    else:
+        n_head_kv, head0 = c["KV"], 0
+    L, n = c["L"], c["n"]
+    units = L * n_head_kv
+
+    td = tempfile.mkdtemp()
+    stats_path = write_stats(c, td)
+    st = tria_b200.load(stats_path)
+    ctx = tria_b200.Context(st, dev.index)
+    src = devcache.DeviceCache(c["type"], L, n_head_kv, c["hd"], n, dev, head0=head0)
+    dst = devcache.DeviceCache(c["type"], L, n_head_kv, c["hd"], n, dev, head0=head0)
+    src.fill_synthetic(seed=1000 + rank)
+    n_rows = np.full(units, n, np.int32)
+    params = tria_b200.EvictParams(n, budget, c["ramp"], 0, 0, 0)
+    sv, dv = src.view(shared_pos=True), dst.view()
+    stream = torch.cuda.Stream(device=dev)
+    keep = workloads.layer_keep(n, budget, c["ramp"])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    clocks = ClockSampler(dev.index)
+    with clocks:
+        with torch.cuda.stream(stream):
+            t_w = time.perf_counter()
+            i = 0
+            while i < args.warmup or time.perf_counter() - t_w < 0.3:
+                ctx.evict(sv, dv, n_rows, params, stream=stream)
+                i += 1
+                if i % 8 == 0:
+                    stream.synchronize()
+            stream.synchronize()
+            r, counts = ctx.get_n_kv(units)
+            assert (counts == keep).all(), (counts[:8], keep)
+
+            barrier()
+            torch.cuda.synchronize()
+            l0 = ctx.launches()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                ctx.evict(sv, dv, n_rows, params, stream=stream)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            launches = ctx.launches() - l0
+            ms = e0.elapsed_time(e1) / args.steps
+    clk = clocks.summary()
+    ms_max = max_over_ranks(ms)
+
+    # stage timing (CUDA events between stages, same workload)
+    ctx.set_timing(True)
+    acc = {}
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, min(args.steps, 50))):
+            ctx.evict(sv, dv, n_rows, params, stream=stream)
+            for k, v in ctx.stage_ms().items():
+                acc.setdefault(k, []).append(v)
+    ctx.set_timing(False)
+    stage = {k: statistics.median(v) for k, v in acc.items()}
+
+    # end to end through the C ABI with host buffers: pinned K, V, positions ->
+    # device, evict, compacted rows + counts -> host, every step
+    e2e = None
+    if not args.no_e2e:
+        hk = torch.empty(src.k.shape, dtype=torch.uint8, pin_memory=True)
+        hv = torch.empty(src.v.shape, dtype=torch.uint8, pin_memory=True)
+        hp = torch.empty((n,), dtype=torch.int32, pin_memory=True)
+        hk.copy_(src.k)
+        hv.copy_(src.v)
+        hp.copy_(src.pos_shared)
+        ok_k = torch.empty((L, keep, src.k.shape[2]), dtype=torch.uint8, pin_memory=True)
+        ok_v = torch.empty_like(ok_k, pin_memory=True)
+        ok_p = torch.empty((L, n_head_kv, keep), dtype=torch.int32, pin_memory=True)
+        h2d = hk.numel() + hv.numel() + hp.numel() * 4
+        d2h = ok_k.numel() + ok_v.numel() + ok_p.numel() * 4 + units * 4
+        e2e_steps = max(2, min(args.steps, 10))
+
+        def e2e_step():
+            src.k.copy_(hk, non_blocking=True)
+            src.v.copy_(hv, non_blocking=True)
+            src.pos_shared.copy_(hp, non_blocking=True)
+            ctx.evict(sv, dv, n_rows, params, stream=stream)
+            ok_k.copy_(dst.k[:, :keep], non_blocking=True)
+            ok_v.copy_(dst.v[:, :keep], non_blocking=True)
+            ok_p.copy_(dst.pos[:, :, :keep], non_blocking=True)
+            return ctx.get_n_kv(units)
+
+        with torch.cuda.stream(stream):
+            e2e_step()
+            stream.synchronize()
+            barrier()
+            t0 = time.perf_counter()
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            f0.record(stream)
+            for _ in range(e2e_steps):
+                e2e_step()
+            f1.record(stream)
+            stream.synchronize()
+            wall = (time.perf_counter() - t0) / e2e_steps
+            dev_ms = f0.elapsed_time(f1) / e2e_steps
+            barrier()
+        e2e_ms = max_over_ranks(max(wall * 1e3, dev_ms))
+        e2e = {"value": units * n * world / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "path": "tria_evict with pinned host K/V/positions copied in and compacted rows + counts copied out each step"}
+        del hk, hv, hp, ok_k, ok_v, ok_p
+
+    ctx.close()
+    tria_b200.free(st)
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    total_units = units * world
+    value = total_units * n / (ms_max / 1e3)
+    peak, peak_src = measured_peak()
+    sb = score_kernel_bytes(c, units)
+    score_ms = stage.get("score")
+    achieved = sb / (score_ms / 1e3) / 1e9 if score_ms else None
+    wl = args.config
+    traffic = ncu_traffic("k_score_raw", wl)
+    step_b = step_bytes(c, units, keep)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+        "scaling": args.scaling if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "f32" if c["type"] == workloads.TYPE_F16 else "f32 (q8_0 cache)",
+        "data": "synthetic (seeded device fill: N(0,1), 1% outlier dims x8; seeded TRIA v2 stats)",
+        "config": {"workload": describe(args.config, c, budget), "layers": L, "kv_heads": c["KV"],
+                   "heads": c["H"], "head_dim": c["hd"], "rows": n, "kept": keep,
+                   "shard": f"{n_head_kv} kv heads x {L} layers per rank",
+                   "l2": "inputs larger than L2 (no flush)"},
+        "roofline": {"bound": "hbm", "kernel": "k_score_raw", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
+                     "traffic": traffic, "peak_source": f"{peak_src} hbm_gbs",
+                     "algorithmic_bytes_per_launch": sb, "launch_ms": score_ms},
+        "step_roofline": {"bytes_per_step": step_b, "achieved": step_b / (ms / 1e3) / 1e9,
+                          "frac": step_b / (ms / 1e3) / 1e9 / peak, "unit": "GB/s"},
+        "stage_ms": stage,
+        "clocks": clk,
+        "gpu_launches": int(launches),
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu:
+        try:
+            threads = len(os.sched_getaffinity(0))
+            n_s = min(units, max(1, threads))
+            rate, dt, th, kind = cpu_step_rate(c, stats_path, n_s, seed=7, threads=threads)
+            line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": th, "kind": kind,
+                                    "sample": f"{n_s} (layer, kv-head) units x {n} rows of the same "
+                                              f"workload (seeded numpy data), {dt:.1f} s wall"}
+        except Exception as e:  # pragma: no cover
+            line["cpu_baseline"] = {"value": None, "unit": UNIT, "error": repr(e)}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,237 @@
+/*
+ * triattention.h - TriAttention KV-cache eviction step for NVIDIA B200 (sm_100a).
+ *
+ * Drop-in for the reference C API of triattention-ggml (triattention.h there):
+ * the four reference entry points and the two public structs keep their names,
+ * signatures, layouts and semantics.  The eviction step itself (score every
+ * cached row, select the rows to keep against the budget and ramp, compact the
+ * K/V cache) runs as hand-written CUDA kernels behind the tria_* device-path
+ * functions declared below.
+ *
+ * Conventions of the device path:
+ *   - every function returns an int status (TRIA_OK == 0, negative on error);
+ *     tria_last_error() gives a message for the calling thread;
+ *   - work is stream-ordered on the cudaStream_t passed as `void *stream`
+ *     (NULL = legacy default stream); nothing synchronises unless stated;
+ *   - caches, positions and outputs are caller-owned device memory; a context
+ *     owns only its scratch, the uploaded stats and the delta table;
+ *   - one context per device; calls on one context must not overlap in time
+ *     on different streams (they share scratch).
+ */
+#ifndef TRIATTENTION_H
+#define TRIATTENTION_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#define TRIA_MAGIC       0x54524941
+#define TRIA_HEADER_SIZE 64
+#define TRIA_N_OFFSETS   17
+
+#if defined(__GNUC__)
+#define TRIA_API __attribute__((visibility("default")))
+#else
+#define TRIA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Per-head calibration stats.  Layout of triattention.h:30-36 (reference). */
+struct tria_head_stats {
+    float *q_mean_real;   /* [fc] */
+    float *q_mean_imag;   /* [fc] */
+    float *q_abs_mean;    /* [fc] */
+    float *qma;           /* [fc] |E[q_f]| */
+};
+
+/* Full calibration data.  Layout of triattention.h:38-50 (reference). */
+struct tria_stats {
+    uint32_t num_layers;
+    uint32_t num_heads;
+    uint32_t num_kv_heads;
+    uint32_t head_dim;
+    uint32_t freq_count;
+    float    rope_theta;
+    float    attn_scale;
+    float   *layer_budget_scales;      /* [num_layers] */
+    float   *omega;                    /* [freq_count] */
+    struct tria_head_stats *heads;     /* [num_layers * num_heads], layer-major */
+};
+
+/* ------------------------------------------------------------------ */
+/* Reference API (kept intact)                                         */
+/* ------------------------------------------------------------------ */
+
+/* Replaces triattention.h:53 / triattention.c:19-83.  Loads a TRIA v1/v2
+ * file; returns NULL (with a message on stderr) on a missing file, bad
+ * magic/version, inconsistent header (fc*2 != head_dim, num_heads not a
+ * multiple of num_kv_heads, zero sizes) or a size that does not match
+ * TRIA_FORMAT.md's formula (short or over-long file). */
+TRIA_API struct tria_stats *tria_load(const char *path);
+
+/* Replaces triattention.h:56 / triattention.c:85-98.  NULL-safe.  Also
+ * releases the device contexts tria_score_kv_head created for `stats`. */
+TRIA_API void tria_free(struct tria_stats *stats);
+
+/* Replaces triattention.h:69-79 / triattention.c:198-253.  Same arguments
+ * (host pointers, fp32 split halves k_pre_real/k_pre_imag [seq_len][fc]) and
+ * the same result: z-normalised (population std, clamp 1e-6) GQA-max scores,
+ * within 1e-4 relative or 1e-5 absolute of the reference.  Runs on the
+ * current CUDA device through a context cached per (stats, device); calls on
+ * one stats object are serialised.  On failure (no GPU, CUDA error) it writes
+ * NaN to out_scores and records tria_last_error(). */
+TRIA_API void tria_score_kv_head(
+    const struct tria_stats *stats,
+    const float *k_pre_real,
+    const float *k_pre_imag,
+    const int   *key_pos,
+    int          cur_pos,
+    int          seq_len,
+    int          layer_idx,
+    int          kv_head_idx,
+    float       *out_scores);
+
+/* triattention.h:85-89, unchanged: max(1, (int)(base_budget * scale[layer])). */
+static inline int tria_layer_budget(const struct tria_stats *s, int layer, int base_budget) {
+    float scale = s->layer_budget_scales[layer];
+    int b = (int)(base_budget * scale);
+    return b > 0 ? b : 1;
+}
+
+/* ------------------------------------------------------------------ */
+/* Device path                                                          */
+/* ------------------------------------------------------------------ */
+
+enum tria_status {
+    TRIA_OK              =  0,
+    TRIA_ERR_INVALID     = -1,  /* bad argument or descriptor */
+    TRIA_ERR_CUDA        = -2,  /* CUDA runtime error */
+    TRIA_ERR_NOMEM       = -3,  /* device allocation failed */
+    TRIA_ERR_POSITION    = -4,  /* a key position lies outside [0, cur_pos] */
+    TRIA_ERR_UNSUPPORTED = -5,  /* geometry or cache type not supported */
+    TRIA_ERR_NO_DEVICE   = -6   /* no CUDA device / not an sm_100 device */
+};
+
+/* Cache element types (ggml type ids). */
+enum tria_kv_type {
+    TRIA_TYPE_F16  = 1,   /* head row = head_dim f16 */
+    TRIA_TYPE_Q8_0 = 8    /* head row = head_dim/32 blocks {f16 d; int8 q[32]} (34 B) */
+};
+
+typedef struct tria_ctx tria_ctx;
+
+/* View of a KV cache (or of one shard of it) in device memory.  Row r of kv
+ * head h in layer l starts at  k[l] + r*cell_stride + h*head_stride  (same for
+ * v).  llama.cpp's layout is cell_stride = n_head_kv*row_bytes, head_stride =
+ * row_bytes; head-major layouts use head_stride = n_cells*row_bytes,
+ * cell_stride = row_bytes.  Bases must be 16-byte aligned; strides and row
+ * bytes must be multiples of 4.  Positions are int32 per row: [n_layer]
+ * [n_head_kv][n_cells] when pos_shared == 0, or one [n_cells] array shared by
+ * every (layer, head) when pos_shared != 0 (llama.cpp cells before the first
+ * per-head compaction).  Layer l of the view is model layer layer0 + l, head
+ * h is model kv head head0 + h (stats lookup). */
+struct tria_kv_view {
+    int32_t  type;          /* enum tria_kv_type */
+    int32_t  n_layer;
+    int32_t  layer0;
+    int32_t  n_head_kv;
+    int32_t  head0;
+    int32_t  n_cells;       /* capacity (rows) per (layer, head) */
+    int64_t  cell_stride;   /* bytes */
+    int64_t  head_stride;   /* bytes */
+    void * const *k;        /* host array [n_layer] of device pointers */
+    void * const *v;        /* host array [n_layer] of device pointers, or NULL (K only) */
+    int32_t *pos;           /* device */
+    int32_t  pos_shared;
+    int32_t  reserved;
+};
+
+/* Eviction policy of one step.  The kept count of a (layer, kv-head) with n
+ * rows is  B_l = tria_layer_budget(stats, layer, budget),
+ *          keep = n                               if n <= B_l
+ *               = n - floor(ramp_pct*(n - B_l)/100) otherwise,
+ * raised to the number of protected rows (window/sink) and capped at n.
+ * Rows are ranked by (score desc, row asc); the best `keep` are kept, in row
+ * order.  The ramp stages of the reference runtime are 10, 20, 40, 80, 100. */
+struct tria_evict_params {
+    int32_t cur_pos;     /* trigger (decode) position; every key position must be <= cur_pos */
+    int32_t budget;      /* base budget in rows per (layer, kv-head), before the layer scale */
+    int32_t ramp_pct;    /* 0..100 */
+    int32_t window;      /* rows with cur_pos - pos < window are always kept (0 = none) */
+    int32_t sink;        /* rows with pos < sink are always kept (0 = none) */
+    int32_t reserved;
+};
+
+TRIA_API const char *tria_status_str(int status);
+TRIA_API const char *tria_last_error(void);
+
+/* Create a context on `device`: uploads the stats (per-head q-centre, residual
+ * norm term, omega) and allocates its scratch lazily.  New. */
+TRIA_API int  tria_ctx_create(const struct tria_stats *stats, int device, tria_ctx **out);
+TRIA_API void tria_ctx_destroy(tria_ctx *ctx);
+
+/* Score every row of every (layer, head) of `kv` at trigger position cur_pos.
+ * n_rows: host [n_layer*n_head_kv] rows per unit.  scores: device
+ * [n_layer*n_head_kv][n_cells] fp32, the GQA-max z-scores of
+ * tria_score_kv_head.  The device counterpart of calling the reference's
+ * tria_score_kv_head (triattention.c:198-253) once per (layer, kv-head). */
+TRIA_API int tria_score(tria_ctx *ctx, const struct tria_kv_view *kv, const int32_t *n_rows,
+                        int32_t cur_pos, float *scores, void *stream);
+
+/* Select the rows to keep from `scores` (layout of tria_score): writes, per
+ * unit, kept row indices in ascending order to kept_idx [units][n_cells] and
+ * their count to n_kept [units] (both device).  Positions come from `kv`
+ * (protected rows).  The selection the reference leaves to its runtime
+ * (triattention.h:10 "Select top-B per KV head"; triattention_common.py:109). */
+TRIA_API int tria_select(tria_ctx *ctx, const struct tria_kv_view *kv, const int32_t *n_rows,
+                         const float *scores, const struct tria_evict_params *params,
+                         int32_t *kept_idx, int32_t *n_kept, void *stream);
+
+/* Move kept rows of `src` (K, V and positions) to rows 0..n_kept-1 of `dst`,
+ * in order: a stable stream compaction, byte-exact (q8_0 blocks move intact).
+ * src and dst must not overlap (ping-pong buffers); dst positions are always
+ * per (layer, head).  Geometry (type, n_layer, n_head_kv, strides) must match. */
+TRIA_API int tria_compact(tria_ctx *ctx, const struct tria_kv_view *src,
+                          const struct tria_kv_view *dst, const int32_t *n_rows,
+                          const int32_t *kept_idx, const int32_t *n_kept, void *stream);
+
+/* One whole eviction step (score -> select -> compact) from src into dst.
+ * n_kept_out: device [units] (may be NULL).  The kept counts are also copied
+ * to the context; tria_get_n_kv() returns them after synchronising. */
+TRIA_API int tria_evict(tria_ctx *ctx, const struct tria_kv_view *src,
+                        const struct tria_kv_view *dst, const int32_t *n_rows,
+                        const struct tria_evict_params *params, int32_t *n_kept_out,
+                        void *stream);
+
+/* Rows per (layer, head) after the last tria_evict on `ctx` (waits for it):
+ * writes the per-unit counts to n_kept (host, may be NULL; `cap` entries at
+ * most) and returns their maximum, the cache length a llama.cpp runtime must
+ * keep (README.md:92, "max over sequences").  Negative on error. */
+TRIA_API int tria_get_n_kv(tria_ctx *ctx, int32_t *n_kept, int32_t cap);
+
+/* Stage timing of the following tria_evict calls on `ctx` (off by default):
+ * CUDA events are recorded on the call's stream between the stages. */
+TRIA_API int tria_ctx_set_timing(tria_ctx *ctx, int enable);
+
+/* Device milliseconds of each stage of the last timed tria_evict (waits for
+ * it): ms[0] table extension, ms[1] scoring, ms[2] z-norm statistics,
+ * ms[3] selection, ms[4] compaction.  Returns the number of stages written. */
+TRIA_API int tria_ctx_stage_ms(tria_ctx *ctx, float *ms, int cap);
+
+/* Number of kernels this context has launched so far. */
+TRIA_API int64_t tria_ctx_launches(const tria_ctx *ctx);
+
+/* Device-pointer form of tria_score_kv_head for one (layer, kv-head):
+ * k_re/k_im [n][fc] fp32, key_pos [n] int32, out [n] fp32, all device. */
+TRIA_API int tria_score_kv_head_dev(tria_ctx *ctx, const float *k_re, const float *k_im,
+                                    const int32_t *key_pos, int32_t cur_pos, int32_t n,
+                                    int32_t layer, int32_t kv_head, float *out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRIATTENTION_H */

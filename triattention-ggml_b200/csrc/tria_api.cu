@@ -1,0 +1,871 @@
+/*
+ * tria_api.cu - host side of the C ABI declared in include/triattention.h.
+ *
+ * Owns the device context (uploaded stats, delta table, scratch), validates
+ * cache views, splits them into launches of at most TRIA_MAX_LAYERS layers /
+ * TRIA_MAX_UNITS units, and launches the kernels of tria_kernels.cuh on the
+ * caller's stream.  The reference-signature tria_score_kv_head runs the same
+ * kernels on host buffers through a context cached per (stats, device).
+ */
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "tria_internal.h"
+#include "tria_kernels.cuh"
+
+using namespace tria;
+
+/* ------------------------------------------------------------------ */
+/* Errors                                                               */
+/* ------------------------------------------------------------------ */
+
+static thread_local char g_err[512];
+
+extern "C" void tria_set_error(const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+}
+
+extern "C" TRIA_API const char *tria_last_error(void) { return g_err; }
+
+extern "C" TRIA_API const char *tria_status_str(int st) {
+    switch (st) {
+        case TRIA_OK: return "ok";
+        case TRIA_ERR_INVALID: return "invalid argument";
+        case TRIA_ERR_CUDA: return "CUDA error";
+        case TRIA_ERR_NOMEM: return "device out of memory";
+        case TRIA_ERR_POSITION: return "key position outside [0, cur_pos]";
+        case TRIA_ERR_UNSUPPORTED: return "unsupported geometry";
+        case TRIA_ERR_NO_DEVICE: return "no sm_100 CUDA device";
+        default: return "unknown status";
+    }
+}
+
+#define FAIL(code, ...) do { tria_set_error(__VA_ARGS__); return (code); } while (0)
+#define CUDA_TRY(call) do { cudaError_t e_ = (call); if (e_ != cudaSuccess) \
+    FAIL(e_ == cudaErrorMemoryAllocation ? TRIA_ERR_NOMEM : TRIA_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); } while (0)
+
+/* Restores the caller's current device on scope exit. */
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() { if (prev >= 0) cudaSetDevice(prev); }
+};
+
+/* ------------------------------------------------------------------ */
+/* Context                                                              */
+/* ------------------------------------------------------------------ */
+
+struct tria_ctx {
+    int device = 0;
+    uint32_t L = 0, H = 0, KV = 0, hd = 0, fc = 0, G = 0;
+    std::vector<float> scales;           /* layer budget scales (host) */
+    float *d_q = nullptr;                /* [L][H][3][fc] */
+    float *d_omega = nullptr;            /* [fc] */
+    /* delta table: entries for d in [t_lo, t_lo + t_len), capacity t_cap rows */
+    float2 *d_table = nullptr;
+    int64_t t_lo = 0, t_len = 0, t_cap = 0;
+    /* scratch */
+    uint8_t *d_scratch = nullptr;
+    size_t scratch_cap = 0;
+    float *raw = nullptr;
+    float2 *ms = nullptr;
+    uint32_t *keys = nullptr;
+    int32_t *kept = nullptr;
+    int32_t *cnt = nullptr;
+    int64_t raw_stride = 0, cell_stride = 0;
+    /* host-API staging */
+    uint8_t *d_io = nullptr;
+    size_t io_cap = 0;
+    cudaStream_t own_stream = nullptr;
+    /* status / counts read-back */
+    int32_t *d_status = nullptr;
+    int32_t *h_pinned = nullptr;         /* [0] = status, [1..] counts */
+    int32_t pinned_cap = 0;
+    int32_t last_units = 0;
+    cudaEvent_t ev_done = nullptr;
+    bool have_step = false;
+    /* stage timing (tria_ctx_set_timing) */
+    bool timing = false, have_timing = false;
+    cudaEvent_t ev_stage[6] = {};
+    int64_t launches = 0;
+    std::mutex mu;
+};
+
+static int check_device(int device) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        FAIL(TRIA_ERR_NO_DEVICE, "no CUDA device visible");
+    }
+    if (device < 0 || device >= n) FAIL(TRIA_ERR_INVALID, "device %d out of range (%d devices)", device, n);
+    cudaDeviceProp p;
+    CUDA_TRY(cudaGetDeviceProperties(&p, device));
+    if (p.major != 10 || p.minor != 0)
+        FAIL(TRIA_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", device, p.major, p.minor);
+    return TRIA_OK;
+}
+
+extern "C" TRIA_API void tria_ctx_destroy(tria_ctx *ctx) {
+    if (!ctx) return;
+    {
+        DeviceGuard g(ctx->device);
+        if (ctx->ev_done) cudaEventSynchronize(ctx->ev_done);
+        cudaFree(ctx->d_q);
+        cudaFree(ctx->d_omega);
+        cudaFree(ctx->d_table);
+        cudaFree(ctx->d_scratch);
+        cudaFree(ctx->d_io);
+        cudaFree(ctx->d_status);
+        if (ctx->h_pinned) cudaFreeHost(ctx->h_pinned);
+        if (ctx->ev_done) cudaEventDestroy(ctx->ev_done);
+        for (cudaEvent_t e : ctx->ev_stage) if (e) cudaEventDestroy(e);
+        if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    }
+    delete ctx;
+}
+
+extern "C" TRIA_API int tria_ctx_create(const tria_stats *s, int device, tria_ctx **out) {
+    if (!out) FAIL(TRIA_ERR_INVALID, "tria_ctx_create: null out");
+    *out = nullptr;
+    if (!s || !s->heads || !s->omega || !s->layer_budget_scales)
+        FAIL(TRIA_ERR_INVALID, "tria_ctx_create: null stats");
+    if (s->num_kv_heads == 0 || s->num_heads % s->num_kv_heads || s->freq_count * 2 != s->head_dim)
+        FAIL(TRIA_ERR_INVALID, "tria_ctx_create: inconsistent stats header");
+    const uint32_t G = s->num_heads / s->num_kv_heads;
+    if (s->freq_count > TRIA_MAX_FC || G > TRIA_MAX_GQA)
+        FAIL(TRIA_ERR_UNSUPPORTED, "tria_ctx_create: fc=%u gqa=%u unsupported", s->freq_count, G);
+    int rc = check_device(device);
+    if (rc) return rc;
+    DeviceGuard g(device);
+    tria_ctx *c = new (std::nothrow) tria_ctx;
+    if (!c) FAIL(TRIA_ERR_NOMEM, "tria_ctx_create: host allocation failed");
+    c->device = device;
+    c->L = s->num_layers; c->H = s->num_heads; c->KV = s->num_kv_heads;
+    c->hd = s->head_dim; c->fc = s->freq_count; c->G = G;
+    c->scales.assign(s->layer_budget_scales, s->layer_budget_scales + s->num_layers);
+    const size_t fc = c->fc;
+    std::vector<float> q((size_t)c->L * c->H * 3 * fc);
+    for (size_t h = 0; h < (size_t)c->L * c->H; h++) {
+        const tria_head_stats &hs = s->heads[h];
+        float *dst = &q[h * 3 * fc];
+        for (size_t f = 0; f < fc; f++) {
+            dst[f] = hs.q_mean_real[f];
+            dst[fc + f] = hs.q_mean_imag[f];
+            const float residual = hs.q_abs_mean[f] - hs.qma[f];   /* triattention.c:175-176 */
+            dst[2 * fc + f] = residual > 0.0f ? residual : 0.0f;
+        }
+    }
+    cudaError_t e = cudaMalloc(&c->d_q, q.size() * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemcpy(c->d_q, q.data(), q.size() * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc(&c->d_omega, fc * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemcpy(c->d_omega, s->omega, fc * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc(&c->d_status, sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMemset(c->d_status, 0, sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        tria_ctx_destroy(c);
+        FAIL(e == cudaErrorMemoryAllocation ? TRIA_ERR_NOMEM : TRIA_ERR_CUDA, "tria_ctx_create: %s", cudaGetErrorString(e));
+    }
+    *out = c;
+    return TRIA_OK;
+}
+
+/* Make the delta table cover d in [lo, hi]. */
+static int ensure_table(tria_ctx *c, int64_t lo, int64_t hi, cudaStream_t st) {
+    const int64_t DMAX = (1 << 24) - (1 << 17);
+    if (lo < -DMAX || hi > DMAX) FAIL(TRIA_ERR_UNSUPPORTED, "position delta range [%lld, %lld] too large",
+                                      (long long)lo, (long long)hi);
+    if (hi < lo) return TRIA_OK;
+    const int fc = (int)c->fc;
+    const int64_t t_hi = c->t_lo + c->t_len - 1;
+    if (c->d_table && lo >= c->t_lo && hi <= t_hi) return TRIA_OK;
+    if (c->d_table && lo >= c->t_lo && hi - c->t_lo < c->t_cap) {
+        /* extend upwards inside the allocation */
+        const int64_t n_new = hi - t_hi;
+        const int64_t total = n_new * fc;
+        k_build_table<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+            c->d_table + c->t_len * fc, t_hi + 1, n_new, c->d_omega, fc);
+        CUDA_TRY(cudaGetLastError());
+        c->launches++;
+        c->t_len += n_new;
+        return TRIA_OK;
+    }
+    int64_t new_lo = c->d_table ? std::min(lo, c->t_lo) : lo;
+    int64_t new_hi = c->d_table ? std::max(hi, t_hi) : hi;
+    new_lo = std::min<int64_t>(new_lo, 0);
+    int64_t cap = new_hi - new_lo + 1;
+    cap = std::max<int64_t>(cap + cap / 4, 4096);            /* room to grow with the decode position */
+    float2 *t = nullptr;
+    cudaDeviceSynchronize();
+    CUDA_TRY(cudaMalloc(&t, (size_t)cap * fc * sizeof(float2)));
+    const int64_t n_d = new_hi - new_lo + 1;
+    k_build_table<<<(unsigned)((n_d * fc + 255) / 256), 256, 0, st>>>(t, new_lo, n_d, c->d_omega, fc);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { cudaFree(t); FAIL(TRIA_ERR_CUDA, "table build: %s", cudaGetErrorString(e)); }
+    c->launches++;
+    if (c->d_table) cudaFree(c->d_table);
+    c->d_table = t;
+    c->t_lo = new_lo;
+    c->t_len = n_d;
+    c->t_cap = cap;
+    return TRIA_OK;
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+/* Scratch for `units` units of up to `cells` rows. */
+static int ensure_scratch(tria_ctx *c, int64_t units, int64_t cells, cudaStream_t st) {
+    const int64_t stride = (cells + 63) & ~(int64_t)63;
+    const size_t raw_b = align256((size_t)units * c->G * stride * 4);
+    const size_t ms_b = align256((size_t)units * c->G * sizeof(float2));
+    const size_t key_b = align256((size_t)units * stride * 4);
+    const size_t kept_b = align256((size_t)units * stride * 4);
+    const size_t cnt_b = align256((size_t)units * 4);
+    const size_t need = raw_b + ms_b + key_b + kept_b + cnt_b;
+    if (need > c->scratch_cap) {
+        cudaDeviceSynchronize();      /* earlier calls may still use it, on any stream */
+        if (c->d_scratch) cudaFree(c->d_scratch);
+        c->d_scratch = nullptr;
+        c->scratch_cap = 0;
+        CUDA_TRY(cudaMalloc(&c->d_scratch, need));
+        c->scratch_cap = need;
+    }
+    uint8_t *p = c->d_scratch;
+    c->raw = (float *)p; p += raw_b;
+    c->ms = (float2 *)p; p += ms_b;
+    c->keys = (uint32_t *)p; p += key_b;
+    c->kept = (int32_t *)p; p += kept_b;
+    c->cnt = (int32_t *)p;
+    c->raw_stride = stride;
+    c->cell_stride = stride;
+    if (c->pinned_cap < units + 1) {
+        if (c->h_pinned) { cudaDeviceSynchronize(); cudaFreeHost(c->h_pinned); }
+        c->h_pinned = nullptr;
+        c->pinned_cap = 0;
+        CUDA_TRY(cudaMallocHost(&c->h_pinned, (size_t)(units + 1) * 4));
+        c->pinned_cap = (int32_t)(units + 1);
+    }
+    return TRIA_OK;
+}
+
+/* ------------------------------------------------------------------ */
+/* View validation                                                      */
+/* ------------------------------------------------------------------ */
+
+static int64_t view_row_bytes(int type, int hd) {
+    if (type == TRIA_TYPE_F16) return 2LL * hd;
+    if (type == TRIA_TYPE_Q8_0) return (int64_t)hd / 32 * 34;
+    return -1;
+}
+
+static int validate_view(const tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, const char *what,
+                         bool need_v) {
+    if (!v) FAIL(TRIA_ERR_INVALID, "%s: null view", what);
+    if (v->type != TRIA_TYPE_F16 && v->type != TRIA_TYPE_Q8_0)
+        FAIL(TRIA_ERR_UNSUPPORTED, "%s: cache type %d unsupported", what, v->type);
+    if (v->type == TRIA_TYPE_Q8_0 && c->hd % 32)
+        FAIL(TRIA_ERR_UNSUPPORTED, "%s: q8_0 needs head_dim %% 32 == 0", what);
+    if (v->n_layer < 1 || v->layer0 < 0 || (uint32_t)(v->layer0 + v->n_layer) > c->L)
+        FAIL(TRIA_ERR_INVALID, "%s: layers [%d, %d) outside the stats' %u", what, v->layer0,
+             v->layer0 + v->n_layer, c->L);
+    if (v->n_head_kv < 1 || v->head0 < 0 || (uint32_t)(v->head0 + v->n_head_kv) > c->KV)
+        FAIL(TRIA_ERR_INVALID, "%s: kv heads [%d, %d) outside the stats' %u", what, v->head0,
+             v->head0 + v->n_head_kv, c->KV);
+    if (v->n_cells < 0) FAIL(TRIA_ERR_INVALID, "%s: negative n_cells", what);
+    if (!v->k || !v->pos) FAIL(TRIA_ERR_INVALID, "%s: null k or pos", what);
+    if (need_v && !v->v) FAIL(TRIA_ERR_INVALID, "%s: null v", what);
+    if ((v->cell_stride & 3) || (v->head_stride & 3) || v->cell_stride <= 0 || v->head_stride < 0)
+        FAIL(TRIA_ERR_INVALID, "%s: strides must be positive multiples of 4", what);
+    if ((uintptr_t)v->pos & 3) FAIL(TRIA_ERR_INVALID, "%s: pos misaligned", what);
+    for (int l = 0; l < v->n_layer; l++) {
+        if (!v->k[l] || ((uintptr_t)v->k[l] & 15)) FAIL(TRIA_ERR_INVALID, "%s: k[%d] null or not 16-byte aligned", what, l);
+        if (v->v && (!v->v[l] || ((uintptr_t)v->v[l] & 15)))
+            FAIL(TRIA_ERR_INVALID, "%s: v[%d] null or not 16-byte aligned", what, l);
+    }
+    if (n_rows) {
+        for (int u = 0; u < v->n_layer * v->n_head_kv; u++)
+            if (n_rows[u] < 0 || n_rows[u] > v->n_cells)
+                FAIL(TRIA_ERR_INVALID, "%s: n_rows[%d] = %d outside [0, %d]", what, u, n_rows[u], v->n_cells);
+    }
+    return TRIA_OK;
+}
+
+/* Launch chunks: at most TRIA_MAX_LAYERS layers and TRIA_MAX_UNITS units each. */
+template <class F>
+static int for_layer_chunks(const tria_kv_view *v, F &&fn) {
+    const int per = std::max(1, std::min(TRIA_MAX_LAYERS, TRIA_MAX_UNITS / v->n_head_kv));
+    for (int l0 = 0; l0 < v->n_layer; l0 += per) {
+        int rc = fn(l0, std::min(per, v->n_layer - l0));
+        if (rc) return rc;
+    }
+    return TRIA_OK;
+}
+
+/* ------------------------------------------------------------------ */
+/* Launchers                                                            */
+/* ------------------------------------------------------------------ */
+
+template <int KT, int FC>
+static bool launch_score_fc(int G, dim3 grid, cudaStream_t st, const ScoreArgs &a) {
+    switch (G) {
+        case 1: k_score_raw<KT, FC, 1><<<grid, SCORE_THREADS, 0, st>>>(a); return true;
+        case 2: k_score_raw<KT, FC, 2><<<grid, SCORE_THREADS, 0, st>>>(a); return true;
+        case 4: k_score_raw<KT, FC, 4><<<grid, SCORE_THREADS, 0, st>>>(a); return true;
+        case 5: k_score_raw<KT, FC, 5><<<grid, SCORE_THREADS, 0, st>>>(a); return true;
+        case 6: k_score_raw<KT, FC, 6><<<grid, SCORE_THREADS, 0, st>>>(a); return true;
+        default: return false;
+    }
+}
+
+template <int KT>
+static bool launch_score_kt(int fc, int G, dim3 grid, cudaStream_t st, const ScoreArgs &a) {
+    switch (fc) {
+        case 32: return launch_score_fc<KT, 32>(G, grid, st, a);
+        case 64: return launch_score_fc<KT, 64>(G, grid, st, a);
+        default: return false;
+    }
+}
+
+static int launch_score(tria_ctx *c, int kt, const ScoreArgs &a, int max_rows, cudaStream_t st) {
+    if (max_rows <= 0) return TRIA_OK;
+    dim3 grid((unsigned)((max_rows + SCORE_CHUNK - 1) / SCORE_CHUNK), (unsigned)a.n_layer);
+    bool ok = kt == KT_F16 ? launch_score_kt<KT_F16>((int)c->fc, (int)c->G, grid, st, a)
+            : kt == KT_Q8_0 ? launch_score_kt<KT_Q8_0>((int)c->fc, (int)c->G, grid, st, a)
+                            : launch_score_kt<KT_F32SPLIT>((int)c->fc, (int)c->G, grid, st, a);
+    if (!ok) FAIL(TRIA_ERR_UNSUPPORTED, "score kernel: fc=%u gqa=%u not instantiated", c->fc, c->G);
+    CUDA_TRY(cudaGetLastError());
+    c->launches++;
+    return TRIA_OK;
+}
+
+static void fill_score_args(const tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, int l0, int nl,
+                            int32_t cur_pos, ScoreArgs &a, int &max_rows) {
+    memset(&a, 0, sizeof a);
+    for (int l = 0; l < nl; l++) a.k[l] = (const uint8_t *)v->k[l0 + l];
+    a.cell_stride = v->cell_stride;
+    a.head_stride = v->head_stride;
+    a.pos = v->pos_shared ? v->pos : v->pos + (int64_t)l0 * v->n_head_kv * v->n_cells;
+    a.pos_shared = v->pos_shared ? 1 : 0;
+    a.n_cells = v->n_cells;
+    a.n_layer = nl;
+    a.n_head_kv = v->n_head_kv;
+    a.layer0 = v->layer0 + l0;
+    a.head0 = v->head0;
+    a.cur_pos = cur_pos;
+    a.H = (int32_t)c->H;
+    a.fc = (int32_t)c->fc;
+    a.q = c->d_q;
+    a.table = c->d_table;
+    a.t_lo = c->t_lo;
+    a.t_len = c->t_len;
+    a.raw = c->raw + (int64_t)l0 * v->n_head_kv * c->G * c->raw_stride;
+    a.raw_stride = c->raw_stride;
+    a.status = c->d_status;
+    max_rows = 0;
+    for (int u = 0; u < nl * v->n_head_kv; u++) {
+        a.n_rows[u] = n_rows[(int64_t)l0 * v->n_head_kv + u];
+        max_rows = std::max(max_rows, a.n_rows[u]);
+    }
+}
+
+static int launch_znorm(tria_ctx *c, int64_t unit0, int units, const int32_t *n_rows, cudaStream_t st) {
+    ZArgs z;
+    z.raw = c->raw + unit0 * c->G * c->raw_stride;
+    z.raw_stride = c->raw_stride;
+    z.G = (int32_t)c->G;
+    z.units = units;
+    z.ms = c->ms + unit0 * c->G;
+    for (int u = 0; u < units; u++) z.n_rows[u] = n_rows[unit0 + u];
+    const int chains = units * (int)c->G;
+    k_znorm_seq<<<(chains + 31) / 32, 32, 0, st>>>(z);
+    CUDA_TRY(cudaGetLastError());
+    c->launches++;
+    return TRIA_OK;
+}
+
+/* Raw scores of every unit of `v`. */
+static int run_score(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, int32_t cur_pos, int kt,
+                     cudaStream_t st) {
+    return for_layer_chunks(v, [&](int l0, int nl) -> int {
+        ScoreArgs *a = new (std::nothrow) ScoreArgs;
+        if (!a) FAIL(TRIA_ERR_NOMEM, "host allocation failed");
+        int max_rows = 0;
+        fill_score_args(c, v, n_rows, l0, nl, cur_pos, *a, max_rows);
+        int rc = launch_score(c, kt, *a, max_rows, st);
+        delete a;
+        return rc;
+    });
+}
+
+/* Z-norm statistics of every unit of `v`. */
+static int run_znorm(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, cudaStream_t st) {
+    return for_layer_chunks(v, [&](int l0, int nl) -> int {
+        return launch_znorm(c, (int64_t)l0 * v->n_head_kv, nl * v->n_head_kv, n_rows, st);
+    });
+}
+
+static int run_scoring(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, int32_t cur_pos, int kt,
+                       cudaStream_t st) {
+    int rc = run_score(c, v, n_rows, cur_pos, kt, st);
+    return rc ? rc : run_znorm(c, v, n_rows, st);
+}
+
+static void keep_requests(const tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows,
+                          const tria_evict_params *p, std::vector<int32_t> &keep) {
+    keep.resize((size_t)v->n_layer * v->n_head_kv);
+    for (int l = 0; l < v->n_layer; l++) {
+        const float scale = c->scales[v->layer0 + l];
+        int b = (int)(p->budget * scale);                              /* triattention.h:85-89 */
+        if (b < 1) b = 1;
+        const int ramp = std::min(100, std::max(0, (int)p->ramp_pct));
+        for (int h = 0; h < v->n_head_kv; h++) {
+            const int u = l * v->n_head_kv + h;
+            const int n = n_rows[u];
+            keep[u] = n <= b ? n : n - (int)((int64_t)ramp * (n - b) / 100);
+        }
+    }
+}
+
+static int launch_select(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, const std::vector<int32_t> &keep,
+                         const tria_evict_params *p, bool fused, const float *scores, int32_t *kept_idx,
+                         int64_t kept_stride, int32_t *n_kept, cudaStream_t st) {
+    return for_layer_chunks(v, [&](int l0, int nl) -> int {
+        SelectArgs *a = new (std::nothrow) SelectArgs;
+        if (!a) FAIL(TRIA_ERR_NOMEM, "host allocation failed");
+        memset(a, 0, sizeof *a);
+        const int64_t u0 = (int64_t)l0 * v->n_head_kv;
+        const int units = nl * v->n_head_kv;
+        a->raw = c->raw + u0 * c->G * c->raw_stride;
+        a->raw_stride = c->raw_stride;
+        a->ms = c->ms + u0 * c->G;
+        a->G = (int32_t)c->G;
+        a->scores = scores ? scores + u0 * v->n_cells : nullptr;
+        a->score_stride = v->n_cells;
+        a->pos = v->pos_shared ? v->pos : v->pos + u0 * v->n_cells;
+        a->pos_shared = v->pos_shared ? 1 : 0;
+        a->pos_cells = v->n_cells;
+        a->cur_pos = p->cur_pos;
+        a->window = p->window;
+        a->sink = p->sink;
+        a->keys = c->keys + u0 * c->cell_stride;
+        a->key_stride = c->cell_stride;
+        a->kept_idx = kept_idx + u0 * kept_stride;
+        a->kept_stride = kept_stride;
+        a->n_kept = n_kept + u0;
+        for (int u = 0; u < units; u++) {
+            a->n_rows[u] = n_rows[u0 + u];
+            a->keep_req[u] = keep[u0 + u];
+        }
+        if (fused) k_select<true><<<units, SELECT_THREADS, 0, st>>>(*a);
+        else k_select<false><<<units, SELECT_THREADS, 0, st>>>(*a);
+        delete a;
+        CUDA_TRY(cudaGetLastError());
+        c->launches++;
+        return TRIA_OK;
+    });
+}
+
+static int launch_compact(tria_ctx *c, const tria_kv_view *s, const tria_kv_view *d, const int32_t *n_rows,
+                          const int32_t *kept_idx, int64_t kept_stride, const int32_t *n_kept, cudaStream_t st) {
+    const int64_t rb = view_row_bytes(s->type, (int)c->hd);
+    auto al = [](int64_t x) { return x & 15 ? (x & 7 ? 4 : 8) : 16; };
+    int vec = std::min({al(rb), al(s->cell_stride), al(s->head_stride), al(d->cell_stride), al(d->head_stride)});
+    return for_layer_chunks(s, [&](int l0, int nl) -> int {
+        CompactArgs *a = new (std::nothrow) CompactArgs;
+        if (!a) FAIL(TRIA_ERR_NOMEM, "host allocation failed");
+        memset(a, 0, sizeof *a);
+        const int64_t u0 = (int64_t)l0 * s->n_head_kv;
+        const int units = nl * s->n_head_kv;
+        for (int l = 0; l < nl; l++) {
+            a->ks[l] = (const uint8_t *)s->k[l0 + l];
+            a->kd[l] = (uint8_t *)d->k[l0 + l];
+            if (s->v) { a->vs[l] = (const uint8_t *)s->v[l0 + l]; a->vd[l] = (uint8_t *)d->v[l0 + l]; }
+        }
+        a->cs_s = s->cell_stride; a->hs_s = s->head_stride;
+        a->cs_d = d->cell_stride; a->hs_d = d->head_stride;
+        a->pos_s = s->pos_shared ? s->pos : s->pos + u0 * s->n_cells;
+        a->pos_shared_s = s->pos_shared ? 1 : 0;
+        a->cells_s = s->n_cells;
+        a->pos_d = d->pos + u0 * d->n_cells;
+        a->cells_d = d->n_cells;
+        a->kept_idx = kept_idx + u0 * kept_stride;
+        a->kept_stride = kept_stride;
+        a->n_kept = n_kept + u0;
+        a->n_head_kv = s->n_head_kv;
+        a->row_bytes = (int32_t)rb;
+        a->has_v = s->v ? 1 : 0;
+        int max_rows = 0;
+        for (int u = 0; u < units; u++) max_rows = std::max(max_rows, n_rows[u0 + u]);
+        const int64_t work = (int64_t)max_rows * (rb / vec);
+        const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 1024));
+        dim3 grid(gx, units);
+        if (max_rows > 0) {
+            if (vec == 16) k_compact<16><<<grid, 256, 0, st>>>(*a);
+            else if (vec == 8) k_compact<8><<<grid, 256, 0, st>>>(*a);
+            else k_compact<4><<<grid, 256, 0, st>>>(*a);
+            c->launches++;
+        }
+        delete a;
+        CUDA_TRY(cudaGetLastError());
+        return TRIA_OK;
+    });
+}
+
+/* ------------------------------------------------------------------ */
+/* Public device-path API                                               */
+/* ------------------------------------------------------------------ */
+
+static int check_positions_range(tria_ctx *c, int32_t cur_pos, cudaStream_t st) {
+    if (cur_pos < 0) FAIL(TRIA_ERR_INVALID, "cur_pos %d < 0", cur_pos);
+    return ensure_table(c, 0, cur_pos, st);
+}
+
+extern "C" TRIA_API int tria_score(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, int32_t cur_pos,
+                                   float *scores, void *stream) {
+    if (!c || !n_rows || !scores) FAIL(TRIA_ERR_INVALID, "tria_score: null argument");
+    int rc = validate_view(c, v, n_rows, "tria_score", false);
+    if (rc) return rc;
+    DeviceGuard g(c->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    if ((rc = check_positions_range(c, cur_pos, st))) return rc;
+    if ((rc = ensure_scratch(c, (int64_t)v->n_layer * v->n_head_kv, v->n_cells, st))) return rc;
+    if ((rc = run_scoring(c, v, n_rows, cur_pos, v->type, st))) return rc;
+    return for_layer_chunks(v, [&](int l0, int nl) -> int {
+        ZmaxArgs z;
+        const int64_t u0 = (int64_t)l0 * v->n_head_kv;
+        const int units = nl * v->n_head_kv;
+        z.raw = c->raw + u0 * c->G * c->raw_stride;
+        z.raw_stride = c->raw_stride;
+        z.ms = c->ms + u0 * c->G;
+        z.G = (int32_t)c->G;
+        z.out = scores + u0 * v->n_cells;
+        z.out_stride = v->n_cells;
+        int max_rows = 0;
+        for (int u = 0; u < units; u++) { z.n_rows[u] = n_rows[u0 + u]; max_rows = std::max(max_rows, z.n_rows[u]); }
+        if (max_rows == 0) return TRIA_OK;
+        dim3 grid((unsigned)std::min((max_rows + 255) / 256, 64), units);
+        k_zmax<<<grid, 256, 0, st>>>(z);
+        CUDA_TRY(cudaGetLastError());
+        c->launches++;
+        return TRIA_OK;
+    });
+}
+
+extern "C" TRIA_API int tria_select(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, const float *scores,
+                                    const tria_evict_params *p, int32_t *kept_idx, int32_t *n_kept, void *stream) {
+    if (!c || !n_rows || !scores || !p || !kept_idx || !n_kept) FAIL(TRIA_ERR_INVALID, "tria_select: null argument");
+    int rc = validate_view(c, v, n_rows, "tria_select", false);
+    if (rc) return rc;
+    DeviceGuard g(c->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    if ((rc = ensure_scratch(c, (int64_t)v->n_layer * v->n_head_kv, v->n_cells, st))) return rc;
+    std::vector<int32_t> keep;
+    keep_requests(c, v, n_rows, p, keep);
+    return launch_select(c, v, n_rows, keep, p, false, scores, kept_idx, v->n_cells, n_kept, st);
+}
+
+static int check_pair(const tria_kv_view *s, const tria_kv_view *d) {
+    if (d->type != s->type || d->n_layer != s->n_layer || d->n_head_kv != s->n_head_kv ||
+        d->layer0 != s->layer0 || d->head0 != s->head0)
+        FAIL(TRIA_ERR_INVALID, "src/dst views differ in type or geometry");
+    if (d->pos_shared) FAIL(TRIA_ERR_INVALID, "dst positions must be per (layer, head)");
+    if ((s->v != nullptr) != (d->v != nullptr)) FAIL(TRIA_ERR_INVALID, "src/dst disagree on V");
+    return TRIA_OK;
+}
+
+extern "C" TRIA_API int tria_compact(tria_ctx *c, const tria_kv_view *s, const tria_kv_view *d, const int32_t *n_rows,
+                                     const int32_t *kept_idx, const int32_t *n_kept, void *stream) {
+    if (!c || !n_rows || !kept_idx || !n_kept) FAIL(TRIA_ERR_INVALID, "tria_compact: null argument");
+    int rc = validate_view(c, s, n_rows, "tria_compact src", false);
+    if (!rc) rc = validate_view(c, d, nullptr, "tria_compact dst", false);
+    if (!rc) rc = check_pair(s, d);
+    if (rc) return rc;
+    for (int64_t u = 0; u < (int64_t)s->n_layer * s->n_head_kv; u++)
+        if (n_rows[u] > d->n_cells)   /* n_kept <= n_rows is only known on the device */
+            FAIL(TRIA_ERR_INVALID, "dst n_cells %d < n_rows[%lld] = %d", d->n_cells, (long long)u, n_rows[u]);
+    DeviceGuard g(c->device);
+    return launch_compact(c, s, d, n_rows, kept_idx, s->n_cells, n_kept, (cudaStream_t)stream);
+}
+
+extern "C" TRIA_API int tria_evict(tria_ctx *c, const tria_kv_view *s, const tria_kv_view *d, const int32_t *n_rows,
+                                   const tria_evict_params *p, int32_t *n_kept_out, void *stream) {
+    if (!c || !n_rows || !p) FAIL(TRIA_ERR_INVALID, "tria_evict: null argument");
+    int rc = validate_view(c, s, n_rows, "tria_evict src", false);
+    if (!rc) rc = validate_view(c, d, nullptr, "tria_evict dst", false);
+    if (!rc) rc = check_pair(s, d);
+    if (rc) return rc;
+    const int64_t units = (int64_t)s->n_layer * s->n_head_kv;
+    for (int64_t u = 0; u < units; u++)
+        if (n_rows[u] > d->n_cells) {
+            /* the kept count is only known on the device; dst must hold the worst case */
+            FAIL(TRIA_ERR_INVALID, "dst n_cells %d < n_rows[%lld] = %d", d->n_cells, (long long)u, n_rows[u]);
+        }
+    DeviceGuard g(c->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    if ((rc = ensure_scratch(c, units, s->n_cells, st))) return rc;
+    std::vector<int32_t> keep;
+    keep_requests(c, s, n_rows, p, keep);
+    int32_t *cnt = n_kept_out ? n_kept_out : c->cnt;
+    auto stage = [&](int i) -> int {
+        if (c->timing) CUDA_TRY(cudaEventRecord(c->ev_stage[i], st));
+        return TRIA_OK;
+    };
+    if ((rc = stage(0))) return rc;
+    if ((rc = check_positions_range(c, p->cur_pos, st))) return rc;
+    if ((rc = stage(1))) return rc;
+    if ((rc = run_score(c, s, n_rows, p->cur_pos, s->type, st))) return rc;
+    if ((rc = stage(2))) return rc;
+    if ((rc = run_znorm(c, s, n_rows, st))) return rc;
+    if ((rc = stage(3))) return rc;
+    if ((rc = launch_select(c, s, n_rows, keep, p, true, nullptr, c->kept, c->cell_stride, cnt, st))) return rc;
+    if ((rc = stage(4))) return rc;
+    if ((rc = launch_compact(c, s, d, n_rows, c->kept, c->cell_stride, cnt, st))) return rc;
+    if ((rc = stage(5))) return rc;
+    c->have_timing = c->timing;
+    CUDA_TRY(cudaMemcpyAsync(c->h_pinned, c->d_status, 4, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaMemcpyAsync(c->h_pinned + 1, cnt, (size_t)units * 4, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaEventRecord(c->ev_done, st));
+    c->last_units = (int32_t)units;
+    c->have_step = true;
+    return TRIA_OK;
+}
+
+extern "C" TRIA_API int tria_get_n_kv(tria_ctx *c, int32_t *n_kept, int32_t cap) {
+    if (!c) FAIL(TRIA_ERR_INVALID, "tria_get_n_kv: null ctx");
+    if (!c->have_step) return 0;
+    DeviceGuard g(c->device);
+    CUDA_TRY(cudaEventSynchronize(c->ev_done));
+    if (c->h_pinned[0] & ST_POSITION) {
+        cudaMemset(c->d_status, 0, 4);
+        c->h_pinned[0] = 0;
+        FAIL(TRIA_ERR_POSITION, "a key position was outside [0, cur_pos]; that step's output is undefined");
+    }
+    int mx = 0;
+    for (int u = 0; u < c->last_units; u++) {
+        mx = std::max(mx, c->h_pinned[1 + u]);
+        if (n_kept && u < cap) n_kept[u] = c->h_pinned[1 + u];
+    }
+    return mx;
+}
+
+extern "C" TRIA_API int tria_ctx_set_timing(tria_ctx *c, int enable) {
+    if (!c) FAIL(TRIA_ERR_INVALID, "tria_ctx_set_timing: null ctx");
+    DeviceGuard g(c->device);
+    if (enable && !c->ev_stage[0])
+        for (cudaEvent_t &e : c->ev_stage) CUDA_TRY(cudaEventCreate(&e));
+    c->timing = enable != 0;
+    return TRIA_OK;
+}
+
+extern "C" TRIA_API int tria_ctx_stage_ms(tria_ctx *c, float *ms, int cap) {
+    if (!c || !ms) FAIL(TRIA_ERR_INVALID, "tria_ctx_stage_ms: null argument");
+    if (!c->have_timing) return 0;
+    DeviceGuard g(c->device);
+    CUDA_TRY(cudaEventSynchronize(c->ev_stage[5]));
+    int k = 0;
+    for (; k < 5 && k < cap; k++) CUDA_TRY(cudaEventElapsedTime(&ms[k], c->ev_stage[k], c->ev_stage[k + 1]));
+    return k;
+}
+
+extern "C" TRIA_API int64_t tria_ctx_launches(const tria_ctx *c) { return c ? c->launches : -1; }
+
+/* Score one (layer, kv-head) from fp32 split halves in device memory; the
+ * delta range [dlo, dhi] must already be covered by the table. */
+static int score_split(tria_ctx *c, const float *k_re, const float *k_im, const int32_t *pos, int32_t cur_pos,
+                       int32_t n, int32_t layer, int32_t kvh, float *out, cudaStream_t st) {
+    if (layer < 0 || (uint32_t)layer >= c->L || kvh < 0 || (uint32_t)kvh >= c->KV)
+        FAIL(TRIA_ERR_INVALID, "layer %d / kv head %d out of range", layer, kvh);
+    if (n <= 0) return TRIA_OK;
+    int rc = ensure_scratch(c, 1, n, st);
+    if (rc) return rc;
+    ScoreArgs *a = new (std::nothrow) ScoreArgs;
+    if (!a) FAIL(TRIA_ERR_NOMEM, "host allocation failed");
+    memset(a, 0, sizeof *a);
+    a->k[0] = (const uint8_t *)k_re;
+    a->kim = (const uint8_t *)k_im;
+    a->cell_stride = (int64_t)c->fc * 4;
+    a->head_stride = 0;
+    a->pos = pos;
+    a->pos_shared = 1;
+    a->n_cells = n;
+    a->n_layer = 1;
+    a->n_head_kv = 1;
+    a->layer0 = layer;
+    a->head0 = kvh;
+    a->cur_pos = cur_pos;
+    a->H = (int32_t)c->H;
+    a->fc = (int32_t)c->fc;
+    a->q = c->d_q;
+    a->table = c->d_table;
+    a->t_lo = c->t_lo;
+    a->t_len = c->t_len;
+    a->raw = c->raw;
+    a->raw_stride = c->raw_stride;
+    a->status = c->d_status;
+    a->n_rows[0] = n;
+    rc = launch_score(c, KT_F32SPLIT, *a, n, st);
+    delete a;
+    if (rc) return rc;
+    int32_t nr[1] = {n};
+    if ((rc = launch_znorm(c, 0, 1, nr, st))) return rc;
+    ZmaxArgs z;
+    z.raw = c->raw;
+    z.raw_stride = c->raw_stride;
+    z.ms = c->ms;
+    z.G = (int32_t)c->G;
+    z.out = out;
+    z.out_stride = n;
+    z.n_rows[0] = n;
+    k_zmax<<<dim3((unsigned)std::min((n + 255) / 256, 256), 1), 256, 0, st>>>(z);
+    CUDA_TRY(cudaGetLastError());
+    c->launches++;
+    return TRIA_OK;
+}
+
+__global__ void k_pos_minmax(const int32_t *pos, int n, int32_t *mm) {
+    int lo = INT32_MAX, hi = INT32_MIN;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        lo = min(lo, pos[i]);
+        hi = max(hi, pos[i]);
+    }
+    atomicMin(&mm[0], lo);
+    atomicMax(&mm[1], hi);
+}
+
+extern "C" TRIA_API int tria_score_kv_head_dev(tria_ctx *c, const float *k_re, const float *k_im,
+                                               const int32_t *key_pos, int32_t cur_pos, int32_t n, int32_t layer,
+                                               int32_t kv_head, float *out, void *stream) {
+    if (!c || (n > 0 && (!k_re || !k_im || !key_pos || !out))) FAIL(TRIA_ERR_INVALID, "tria_score_kv_head_dev: null argument");
+    if (n < 0) FAIL(TRIA_ERR_INVALID, "negative n");
+    if (n == 0) return TRIA_OK;
+    if (((uintptr_t)k_re & 15) || ((uintptr_t)k_im & 15)) FAIL(TRIA_ERR_INVALID, "k_re/k_im must be 16-byte aligned");
+    DeviceGuard g(c->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    /* the delta range is data-dependent: read the position extremes once */
+    int rc = ensure_scratch(c, 1, n, st);
+    if (rc) return rc;
+    int32_t init[2] = {INT32_MAX, INT32_MIN};
+    CUDA_TRY(cudaMemcpyAsync(c->cnt, init, 8, cudaMemcpyHostToDevice, st));
+    k_pos_minmax<<<std::min((n + 255) / 256, 128), 256, 0, st>>>(key_pos, n, c->cnt);
+    CUDA_TRY(cudaGetLastError());
+    int32_t mm[2];
+    CUDA_TRY(cudaMemcpyAsync(mm, c->cnt, 8, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    if ((rc = ensure_table(c, (int64_t)cur_pos - mm[1], (int64_t)cur_pos - mm[0], st))) return rc;
+    return score_split(c, k_re, k_im, key_pos, cur_pos, n, layer, kv_head, out, st);
+}
+
+/* ------------------------------------------------------------------ */
+/* Reference-signature entry point                                      */
+/* ------------------------------------------------------------------ */
+
+struct RegEntry {
+    const tria_stats *stats;
+    int device;
+    tria_ctx *ctx;
+};
+static std::mutex g_reg_mu;
+static std::vector<RegEntry> g_reg;
+
+extern "C" void tria_release_stats_contexts(const tria_stats *s) {
+    std::vector<tria_ctx *> dead;
+    {
+        std::lock_guard<std::mutex> lk(g_reg_mu);
+        for (size_t i = 0; i < g_reg.size();) {
+            if (g_reg[i].stats == s) { dead.push_back(g_reg[i].ctx); g_reg.erase(g_reg.begin() + i); }
+            else i++;
+        }
+    }
+    for (tria_ctx *c : dead) tria_ctx_destroy(c);
+}
+
+static tria_ctx *registry_get(const tria_stats *s, int device, int *rc) {
+    std::lock_guard<std::mutex> lk(g_reg_mu);
+    for (auto &e : g_reg)
+        if (e.stats == s && e.device == device) return e.ctx;
+    tria_ctx *c = nullptr;
+    *rc = tria_ctx_create(s, device, &c);
+    if (*rc) return nullptr;
+    g_reg.push_back({s, device, c});
+    return c;
+}
+
+static int score_host(tria_ctx *c, const float *k_re, const float *k_im, const int *key_pos, int cur_pos, int n,
+                      int layer, int kvh, float *out) {
+    if (n <= 0) return TRIA_OK;
+    DeviceGuard g(c->device);
+    cudaStream_t st = c->own_stream;
+    int64_t dlo = INT64_MAX, dhi = INT64_MIN;
+    for (int r = 0; r < n; r++) {
+        const int64_t d = (int64_t)cur_pos - key_pos[r];
+        dlo = std::min(dlo, d);
+        dhi = std::max(dhi, d);
+    }
+    int rc = ensure_table(c, dlo, dhi, st);
+    if (rc) return rc;
+    const size_t fb = (size_t)n * c->fc * 4;
+    const size_t need = 2 * align256(fb) + 2 * align256((size_t)n * 4);
+    if (need > c->io_cap) {
+        cudaStreamSynchronize(st);
+        cudaFree(c->d_io);
+        c->d_io = nullptr;
+        c->io_cap = 0;
+        CUDA_TRY(cudaMalloc(&c->d_io, need));
+        c->io_cap = need;
+    }
+    float *dre = (float *)c->d_io;
+    float *dim = (float *)(c->d_io + align256(fb));
+    int32_t *dpos = (int32_t *)(c->d_io + 2 * align256(fb));
+    float *dout = (float *)(c->d_io + 2 * align256(fb) + align256((size_t)n * 4));
+    CUDA_TRY(cudaMemcpyAsync(dre, k_re, fb, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(dim, k_im, fb, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(dpos, key_pos, (size_t)n * 4, cudaMemcpyHostToDevice, st));
+    if ((rc = score_split(c, dre, dim, dpos, cur_pos, n, layer, kvh, dout, st))) return rc;
+    CUDA_TRY(cudaMemcpyAsync(out, dout, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+    int32_t status = 0;
+    CUDA_TRY(cudaMemcpyAsync(&status, c->d_status, 4, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    if (status) {
+        cudaMemset(c->d_status, 0, 4);
+        FAIL(TRIA_ERR_POSITION, "delta outside the table");
+    }
+    return TRIA_OK;
+}
+
+extern "C" TRIA_API void tria_score_kv_head(const tria_stats *stats, const float *k_pre_real, const float *k_pre_imag,
+                                            const int *key_pos, int cur_pos, int seq_len, int layer_idx,
+                                            int kv_head_idx, float *out_scores) {
+    int rc = TRIA_ERR_INVALID;
+    if (stats && k_pre_real && k_pre_imag && key_pos && out_scores && seq_len >= 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); dev = 0; }
+        tria_ctx *c = registry_get(stats, dev, &rc);
+        if (c) {
+            std::lock_guard<std::mutex> lk(c->mu);
+            rc = score_host(c, k_pre_real, k_pre_imag, key_pos, cur_pos, seq_len, layer_idx, kv_head_idx, out_scores);
+        }
+    } else {
+        tria_set_error("tria_score_kv_head: null argument");
+    }
+    if (rc != TRIA_OK) {
+        fprintf(stderr, "tria_score_kv_head: %s\n", g_err);
+        if (out_scores)
+            for (int r = 0; r < seq_len; r++) out_scores[r] = NAN;
+    }
+}

@@ -1,0 +1,25 @@
+/* tria_internal.h - declarations shared by the loader (C) and the device path (CUDA C++). */
+#ifndef TRIA_INTERNAL_H
+#define TRIA_INTERNAL_H
+
+#include "triattention.h"
+
+#define TRIA_MAX_FC         128     /* frequency pairs per head (head_dim <= 256) */
+#define TRIA_MAX_GQA        16      /* query heads per kv head */
+#define TRIA_MAX_LAYERS     128     /* layers per kernel launch (views are split above) */
+#define TRIA_MAX_UNITS      2048    /* (layer, kv-head) units per kernel launch */
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Record a printf-style message for tria_last_error() of this thread. */
+void tria_set_error(const char *fmt, ...);
+
+/* Destroy the device contexts tria_score_kv_head cached for `stats`. */
+void tria_release_stats_contexts(const struct tria_stats *stats);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,524 @@
+/*
+ * tria_kernels.cuh - sm_100a kernels of the TriAttention eviction step.
+ *
+ * The reference scores one (layer, kv-head) at a time on the CPU
+ * (triattention.c:198-253): a per-row cos/sin table of n x 17 x fc sincosf
+ * calls, one pass per query head over fc x 17 products, a sequential fp32
+ * z-norm per query head, then a max over the GQA group.  Here the step is:
+ *
+ *   k_build_table  T[d][f] = sum_o (cos, sin)(fl(fl(d + 2^o) * omega_f))
+ *                  The angle is the reference's exact fp32 value; cos/sin are
+ *                  evaluated in double and summed over the 17 offsets, so the
+ *                  table depends only on the integer delta d = cur_pos - pos.
+ *                  It is built once per context and reused by every layer,
+ *                  head and step (like a RoPE cache).
+ *   k_score_raw    streams the K cache once.  Per row it forms
+ *                     X_f = C kr + S ki,  Y_f = C ki - S kr,  |k_f|
+ *                  and for each query head g of the group
+ *                     raw_g = (sum_f qr_gf X_f + qi_gf Y_f) / 17 + sum_f res_gf |k_f|
+ *                  which is triattention.c:156-192 with the offset sum moved
+ *                  into the table (rel_r cos - rel_i sin summed over o).
+ *   k_znorm_seq    mean and variance as the reference's sequential fp32 chains
+ *                  (triattention.c:228-236), IEEE div/sqrt, std clamp 1e-6.
+ *   k_select       z-score max over the group (triattention.c:240-247), an
+ *                  order-preserving 32-bit key, 8-bit radix select of the
+ *                  keep-th largest key, ties to the lowest rows, and an
+ *                  ordered block scan that writes kept row indices in order.
+ *   k_compact      stable gather of kept K/V rows and positions into the
+ *                  ping-pong buffer, vectorised, byte-exact.
+ *
+ * No tensor cores: this is a streaming fp32 reduction bounded by HBM.
+ */
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "tria_internal.h"
+
+namespace tria {
+
+enum : int { KT_F32SPLIT = 0, KT_F16 = TRIA_TYPE_F16, KT_Q8_0 = TRIA_TYPE_Q8_0 };
+enum : int { ST_POSITION = 1 };
+
+constexpr int N_OFF = 17;
+constexpr int SCORE_THREADS = 256;
+constexpr int SCORE_CHUNK = 256;       /* cells per CTA (per layer) */
+constexpr int SELECT_THREADS = 1024;
+
+/* ------------------------------------------------------------------ */
+/* Delta table                                                          */
+/* ------------------------------------------------------------------ */
+
+__global__ void k_build_table(float2 *__restrict__ T, int64_t d_lo, int64_t n_d,
+                              const float *__restrict__ omega, int fc) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_d * fc) return;
+    int64_t di = i / fc;
+    int f = (int)(i - di * fc);
+    float base = (float)(d_lo + di);           /* (float)(cur_pos - key_pos), exact below 2^24 */
+    float w = omega[f];
+    double c = 0.0, s = 0.0;
+#pragma unroll
+    for (int o = 0; o < N_OFF; o++) {
+        float delta = __fadd_rn(base, (float)(1 << o));
+        float ang = __fmul_rn(delta, w);
+        double sd, cd;
+        sincos((double)ang, &sd, &cd);
+        c += cd;
+        s += sd;
+    }
+    T[i] = make_float2((float)c, (float)s);
+}
+
+/* ------------------------------------------------------------------ */
+/* Scoring                                                              */
+/* ------------------------------------------------------------------ */
+
+struct ScoreArgs {
+    const uint8_t *k[TRIA_MAX_LAYERS];   /* per-layer K base (F32SPLIT: real plane) */
+    const uint8_t *kim;                   /* F32SPLIT: imag plane */
+    int64_t cell_stride, head_stride;     /* bytes */
+    const int32_t *pos;
+    int32_t pos_shared, n_cells, n_layer, n_head_kv, layer0, head0, cur_pos, H, fc;
+    const float *q;                       /* [L][H][3][fc]: qr, qi, max(0, qam - qma) */
+    const float2 *table;                  /* [t_len][fc] */
+    int64_t t_lo, t_len;
+    float *raw;                           /* [units*G][raw_stride] */
+    int64_t raw_stride;
+    int32_t *status;
+    int32_t n_rows[TRIA_MAX_UNITS];
+};
+
+__device__ __forceinline__ float sqrt_approx(float x) {
+    float y;
+    asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+/* Load this lane's FPL pairs (dims [d0, d0+FPL) and [fc+d0, fc+d0+FPL)) of one row. */
+template <int KT, int FPL>
+__device__ __forceinline__ void load_pairs(const ScoreArgs &a, const uint8_t *row, int64_t cell,
+                                           int d0, float (&kr)[FPL], float (&ki)[FPL]) {
+    if constexpr (KT == KT_F32SPLIT) {
+        const float *pr = reinterpret_cast<const float *>(a.k[0] + cell * a.cell_stride) + d0;
+        const float *pi = reinterpret_cast<const float *>(a.kim + cell * a.cell_stride) + d0;
+        if constexpr (FPL % 4 == 0) {
+#pragma unroll
+            for (int t = 0; t < FPL / 4; t++) {
+                float4 x = reinterpret_cast<const float4 *>(pr)[t];
+                float4 y = reinterpret_cast<const float4 *>(pi)[t];
+                kr[4 * t] = x.x; kr[4 * t + 1] = x.y; kr[4 * t + 2] = x.z; kr[4 * t + 3] = x.w;
+                ki[4 * t] = y.x; ki[4 * t + 1] = y.y; ki[4 * t + 2] = y.z; ki[4 * t + 3] = y.w;
+            }
+        } else {
+#pragma unroll
+            for (int t = 0; t < FPL; t++) { kr[t] = pr[t]; ki[t] = pi[t]; }
+        }
+    } else if constexpr (KT == KT_F16) {
+        const __half2 *pr = reinterpret_cast<const __half2 *>(row + 2 * d0);
+        const __half2 *pi = reinterpret_cast<const __half2 *>(row + 2 * (a.fc + d0));
+#pragma unroll
+        for (int t = 0; t < FPL / 2; t++) {
+            float2 x = __half22float2(pr[t]);
+            float2 y = __half22float2(pi[t]);
+            kr[2 * t] = x.x; kr[2 * t + 1] = x.y;
+            ki[2 * t] = y.x; ki[2 * t + 1] = y.y;
+        }
+    } else {   /* q8_0: ggml block {f16 d; int8 q[32]}; FPL divides 32 so a lane stays in one block */
+        auto deq = [&](int dim0, float (&out)[FPL]) {
+            const uint8_t *blk = row + (dim0 >> 5) * 34;
+            float d = __half2float(*reinterpret_cast<const __half *>(blk));
+            const char2 *q2 = reinterpret_cast<const char2 *>(blk + 2 + (dim0 & 31));
+#pragma unroll
+            for (int t = 0; t < FPL / 2; t++) {
+                char2 v = q2[t];
+                out[2 * t] = (float)v.x * d;
+                out[2 * t + 1] = (float)v.y * d;
+            }
+        };
+        deq(d0, kr);
+        deq(a.fc + d0, ki);
+    }
+}
+
+/* One CTA = one layer x SCORE_CHUNK cells; warp w scores kv heads w, w+8, ...
+ * LPR lanes share a row, each owning FPL consecutive frequency pairs. */
+template <int KT, int FC, int G>
+__global__ void __launch_bounds__(SCORE_THREADS) k_score_raw(const ScoreArgs a) {
+    constexpr int FPL = FC <= 64 ? FC / 8 : 8;
+    constexpr int LPR = FC / FPL;
+    constexpr int RPW = 32 / LPR;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int j = lane % LPR, slot = lane / LPR;
+    const int l = blockIdx.y;
+    const int c_begin = blockIdx.x * SCORE_CHUNK;
+    const float inv17 = 1.0f / 17.0f;
+
+    for (int h = warp; h < a.n_head_kv; h += SCORE_THREADS / 32) {
+        const int u = l * a.n_head_kv + h;
+        const int n = a.n_rows[u];
+        const int c_end = min(c_begin + SCORE_CHUNK, n);
+        if (c_begin >= c_end) continue;
+
+        const int ml = a.layer0 + l, mh = a.head0 + h;
+        float qr[G][FPL], qi[G][FPL], qx[G][FPL];
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float *b = a.q + ((size_t)(ml * a.H + mh * G + g) * 3) * FC + j * FPL;
+#pragma unroll
+            for (int t = 0; t < FPL; t++) {
+                qr[g][t] = b[t];
+                qi[g][t] = b[FC + t];
+                qx[g][t] = b[2 * FC + t];
+            }
+        }
+        const uint8_t *kbase = a.k[l] + (int64_t)h * a.head_stride;
+
+        for (int c0 = c_begin; c0 < c_end; c0 += RPW) {
+            const int c = c0 + slot;
+            bool valid = c < c_end;
+            float v[G];
+#pragma unroll
+            for (int g = 0; g < G; g++) v[g] = 0.f;
+            if (valid) {
+                const int p = a.pos[a.pos_shared ? (int64_t)c : (int64_t)u * a.n_cells + c];
+                const int64_t di = (int64_t)a.cur_pos - p - a.t_lo;
+                if (di < 0 || di >= a.t_len) {
+                    atomicOr(a.status, ST_POSITION);
+                    valid = false;
+                } else {
+                    float kr[FPL], ki[FPL];
+                    load_pairs<KT, FPL>(a, kbase + (int64_t)c * a.cell_stride, c, j * FPL, kr, ki);
+                    const float4 *T4 = reinterpret_cast<const float4 *>(a.table + di * FC + j * FPL);
+                    float acc[G], ext[G];
+#pragma unroll
+                    for (int g = 0; g < G; g++) { acc[g] = 0.f; ext[g] = 0.f; }
+#pragma unroll
+                    for (int t2 = 0; t2 < FPL / 2; t2++) {
+                        const float4 cs = T4[t2];      /* (C, S) of pairs 2*t2, 2*t2+1 */
+#pragma unroll
+                        for (int e = 0; e < 2; e++) {
+                            const int t = 2 * t2 + e;
+                            const float C = e ? cs.z : cs.x, S = e ? cs.w : cs.y;
+                            const float X = fmaf(C, kr[t], S * ki[t]);
+                            const float Y = fmaf(C, ki[t], -(S * kr[t]));
+                            const float ka = sqrt_approx(fmaf(kr[t], kr[t], ki[t] * ki[t]));
+#pragma unroll
+                            for (int g = 0; g < G; g++) {
+                                acc[g] = fmaf(qr[g][t], X, acc[g]);
+                                acc[g] = fmaf(qi[g][t], Y, acc[g]);
+                                ext[g] = fmaf(qx[g][t], ka, ext[g]);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int g = 0; g < G; g++) v[g] = fmaf(acc[g], inv17, ext[g]);
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; g++)
+#pragma unroll
+                for (int m = 1; m < LPR; m <<= 1) v[g] += __shfl_xor_sync(0xffffffffu, v[g], m);
+            if (valid && j == 0) {
+#pragma unroll
+                for (int g = 0; g < G; g++) a.raw[((int64_t)u * G + g) * a.raw_stride + c] = v[g];
+            }
+        }
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* Z-norm statistics: sequential fp32, triattention.c:228-238          */
+/* ------------------------------------------------------------------ */
+
+struct ZArgs {
+    const float *raw;
+    int64_t raw_stride;
+    int32_t G, units;
+    float2 *ms;                          /* [units*G] (mean, std) */
+    int32_t n_rows[TRIA_MAX_UNITS];
+};
+
+__global__ void k_znorm_seq(const ZArgs a) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= a.units * a.G) return;
+    const int n = a.n_rows[t / a.G];
+    const float *x = a.raw + (int64_t)t * a.raw_stride;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    const int n4 = n >> 2;
+    float s = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < n4; i++) {
+        const float4 v = x4[i];
+        s = __fadd_rn(s, v.x); s = __fadd_rn(s, v.y);
+        s = __fadd_rn(s, v.z); s = __fadd_rn(s, v.w);
+    }
+    for (int r = n4 * 4; r < n; r++) s = __fadd_rn(s, x[r]);
+    const float mean = __fdiv_rn(s, (float)n);
+    float var = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < n4; i++) {
+        const float4 v = x4[i];
+        float d;
+        d = __fsub_rn(v.x, mean); var = __fadd_rn(var, __fmul_rn(d, d));
+        d = __fsub_rn(v.y, mean); var = __fadd_rn(var, __fmul_rn(d, d));
+        d = __fsub_rn(v.z, mean); var = __fadd_rn(var, __fmul_rn(d, d));
+        d = __fsub_rn(v.w, mean); var = __fadd_rn(var, __fmul_rn(d, d));
+    }
+    for (int r = n4 * 4; r < n; r++) {
+        const float d = __fsub_rn(x[r], mean);
+        var = __fadd_rn(var, __fmul_rn(d, d));
+    }
+    float sd = __fsqrt_rn(__fdiv_rn(var, (float)n));
+    if (sd < 1e-6f) sd = 1e-6f;
+    a.ms[t] = make_float2(mean, sd);
+}
+
+/* z-score of row r, max over the group: triattention.c:240-247 */
+__device__ __forceinline__ float group_zmax(const float *raw, int64_t raw_stride, const float2 *ms,
+                                            int G, int64_t u, int r) {
+    float out = 0.f;
+    for (int g = 0; g < G; g++) {
+        const float2 m = ms[u * G + g];
+        const float z = __fdiv_rn(__fsub_rn(raw[(u * G + g) * raw_stride + r], m.x), m.y);
+        if (g == 0 || z > out) out = z;
+    }
+    return out;
+}
+
+struct ZmaxArgs {
+    const float *raw;
+    int64_t raw_stride;
+    const float2 *ms;
+    int32_t G;
+    float *out;
+    int64_t out_stride;
+    int32_t n_rows[TRIA_MAX_UNITS];
+};
+
+__global__ void k_zmax(const ZmaxArgs a) {
+    const int u = blockIdx.y;
+    const int n = a.n_rows[u];
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n; r += gridDim.x * blockDim.x)
+        a.out[(int64_t)u * a.out_stride + r] = group_zmax(a.raw, a.raw_stride, a.ms, a.G, u, r);
+}
+
+/* ------------------------------------------------------------------ */
+/* Selection                                                            */
+/* ------------------------------------------------------------------ */
+
+/* Order-preserving key: NaN lowest, -0 == +0; protected rows get 0xffffffff. */
+__device__ __forceinline__ uint32_t score_key(float x) {
+    if (x != x) return 0u;
+    if (x == 0.0f) x = 0.0f;
+    const uint32_t u = __float_as_uint(x);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+struct SelectArgs {
+    const float *raw;                 /* fused: raw scores + (mean, std) */
+    int64_t raw_stride;
+    const float2 *ms;
+    int32_t G;
+    const float *scores;              /* direct: final scores */
+    int64_t score_stride;
+    const int32_t *pos;
+    int32_t pos_shared, pos_cells;
+    int32_t cur_pos, window, sink;
+    uint32_t *keys;
+    int64_t key_stride;
+    int32_t *kept_idx;
+    int64_t kept_stride;
+    int32_t *n_kept;
+    int32_t n_rows[TRIA_MAX_UNITS];
+    int32_t keep_req[TRIA_MAX_UNITS];
+};
+
+/* Exclusive block scan of one flag per thread; `total` = number of set flags. */
+__device__ __forceinline__ int block_excl_scan(bool f, int *s_warp, int &total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const unsigned b = __ballot_sync(0xffffffffu, f);
+    const int pre = __popc(b & ((1u << lane) - 1u));
+    if (lane == 0) s_warp[w] = __popc(b);
+    __syncthreads();
+    if (w == 0) {
+        int v = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, v, m);
+            if (lane >= m) v += t;
+        }
+        s_warp[lane] = v;
+    }
+    __syncthreads();
+    const int base = w ? s_warp[w - 1] : 0;
+    total = s_warp[nw - 1];
+    __syncthreads();
+    return base + pre;
+}
+
+__device__ __forceinline__ int block_sum(int v, int *s_warp) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int m = 16; m; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    if (lane == 0) s_warp[w] = v;
+    __syncthreads();
+    int t = 0;
+    for (int i = 0; i < nw; i++) t += s_warp[i];
+    __syncthreads();
+    return t;
+}
+
+template <bool FUSED>
+__global__ void __launch_bounds__(SELECT_THREADS) k_select(const SelectArgs a) {
+    __shared__ int s_hist[256];
+    __shared__ int s_warp[32];
+    __shared__ int s_bc[2];
+    const int u = blockIdx.x, tid = threadIdx.x, bd = blockDim.x;
+    const int n = a.n_rows[u];
+    uint32_t *keys = a.keys + (int64_t)u * a.key_stride;
+    int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
+    const bool prot_on = a.window > 0 || a.sink > 0;
+
+    int prot = 0;
+    for (int r = tid; r < n; r += bd) {
+        float x;
+        if constexpr (FUSED) x = group_zmax(a.raw, a.raw_stride, a.ms, a.G, u, r);
+        else x = a.scores[(int64_t)u * a.score_stride + r];
+        uint32_t k = score_key(x);
+        if (prot_on) {
+            const int p = a.pos[a.pos_shared ? (int64_t)r : (int64_t)u * a.pos_cells + r];
+            if ((a.sink > 0 && p < a.sink) || (a.window > 0 && a.cur_pos - p < a.window)) {
+                k = 0xffffffffu;
+                prot++;
+            }
+        }
+        keys[r] = k;
+    }
+    const int n_prot = prot_on ? block_sum(prot, s_warp) : 0;
+    int keep = a.keep_req[u] > n_prot ? a.keep_req[u] : n_prot;
+    keep = keep > n ? n : (keep < 0 ? 0 : keep);
+    __syncthreads();
+
+    if (keep == n) {                     /* nothing evicted: identity */
+        for (int r = tid; r < n; r += bd) kept[r] = r;
+        if (tid == 0) a.n_kept[u] = keep;
+        return;
+    }
+    if (keep == 0) {
+        if (tid == 0) a.n_kept[u] = 0;
+        return;
+    }
+
+    uint32_t prefix = 0;
+    int need = keep;
+    for (int pass = 0; pass < 4; pass++) {
+        const int shift = 24 - 8 * pass;
+        for (int i = tid; i < 256; i += bd) s_hist[i] = 0;
+        __syncthreads();
+        for (int r = tid; r < n; r += bd) {
+            const uint32_t k = keys[r];
+            if (pass == 0 || ((k ^ prefix) >> (shift + 8)) == 0u) atomicAdd(&s_hist[(k >> shift) & 255u], 1);
+        }
+        __syncthreads();
+        if (tid < 32) {
+            int loc[8], sum = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i++) { loc[i] = s_hist[8 * tid + i]; sum += loc[i]; }
+            int incl = sum;      /* count in bins of this lane and all higher lanes */
+#pragma unroll
+            for (int m = 1; m < 32; m <<= 1) {
+                const int t = __shfl_down_sync(0xffffffffu, incl, m);
+                if (tid + m < 32) incl += t;
+            }
+            const int above = incl - sum;
+            const unsigned bal = __ballot_sync(0xffffffffu, above < need && need <= incl);
+            if (tid == __ffs(bal) - 1) {
+                int acc = above;
+                for (int i = 7; i >= 0; i--) {
+                    if (acc + loc[i] >= need) { s_bc[0] = 8 * tid + i; s_bc[1] = need - acc; break; }
+                    acc += loc[i];
+                }
+            }
+        }
+        __syncthreads();
+        prefix |= (uint32_t)s_bc[0] << shift;
+        need = s_bc[1];
+        __syncthreads();
+    }
+
+    int run_eq = 0, run_kept = 0;
+    for (int base = 0; base < n; base += bd) {
+        const int r = base + tid;
+        const uint32_t k = r < n ? keys[r] : 0u;
+        const bool eq = r < n && k == prefix;
+        int tot_eq, tot_k;
+        const int eq_rank = run_eq + block_excl_scan(eq, s_warp, tot_eq);
+        const bool kp = r < n && (k > prefix || (eq && eq_rank < need));
+        const int dst = run_kept + block_excl_scan(kp, s_warp, tot_k);
+        if (kp) kept[dst] = r;
+        run_eq += tot_eq;
+        run_kept += tot_k;
+    }
+    if (tid == 0) a.n_kept[u] = keep;
+}
+
+/* ------------------------------------------------------------------ */
+/* Compaction                                                           */
+/* ------------------------------------------------------------------ */
+
+struct CompactArgs {
+    const uint8_t *ks[TRIA_MAX_LAYERS];
+    const uint8_t *vs[TRIA_MAX_LAYERS];
+    uint8_t *kd[TRIA_MAX_LAYERS];
+    uint8_t *vd[TRIA_MAX_LAYERS];
+    int64_t cs_s, hs_s, cs_d, hs_d;
+    const int32_t *pos_s;
+    int32_t pos_shared_s, cells_s;
+    int32_t *pos_d;
+    int32_t cells_d;
+    const int32_t *kept_idx;
+    int64_t kept_stride;
+    const int32_t *n_kept;
+    int32_t n_head_kv, row_bytes, has_v;
+};
+
+template <int VEC>
+struct VecT;
+template <> struct VecT<16> { using T = uint4; };
+template <> struct VecT<8> { using T = uint2; };
+template <> struct VecT<4> { using T = uint32_t; };
+
+template <int VEC>
+__global__ void __launch_bounds__(256) k_compact(const CompactArgs a) {
+    using V = typename VecT<VEC>::T;
+    const int u = blockIdx.y;
+    const int l = u / a.n_head_kv, h = u - l * a.n_head_kv;
+    const int nk = a.n_kept[u];
+    const int chunks = a.row_bytes / VEC;
+    const int64_t total = (int64_t)nk * chunks;
+    const int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
+    const uint8_t *ks = a.ks[l] + (int64_t)h * a.hs_s;
+    uint8_t *kd = a.kd[l] + (int64_t)h * a.hs_d;
+    const uint8_t *vs = a.has_v ? a.vs[l] + (int64_t)h * a.hs_s : nullptr;
+    uint8_t *vd = a.has_v ? a.vd[l] + (int64_t)h * a.hs_d : nullptr;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int jrow = (int)(i / chunks);
+        const int c = (int)(i - (int64_t)jrow * chunks);
+        const int r = kept[jrow];
+        const V kv = *reinterpret_cast<const V *>(ks + (int64_t)r * a.cs_s + c * VEC);
+        *reinterpret_cast<V *>(kd + (int64_t)jrow * a.cs_d + c * VEC) = kv;
+        if (vs) {
+            const V vv = *reinterpret_cast<const V *>(vs + (int64_t)r * a.cs_s + c * VEC);
+            *reinterpret_cast<V *>(vd + (int64_t)jrow * a.cs_d + c * VEC) = vv;
+        }
+        if (c == 0)
+            a.pos_d[(int64_t)u * a.cells_d + jrow] =
+                a.pos_s[a.pos_shared_s ? (int64_t)r : (int64_t)u * a.cells_s + r];
+    }
+}
+
+}  // namespace tria

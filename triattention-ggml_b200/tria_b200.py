@@ -1,0 +1,266 @@
+"""ctypes binding of libtriattention_b200.so (include/triattention.h).
+
+The reference's Python side reimplements the scoring math in torch
+(triattention_common.py); this module instead calls the C ABI, so the
+Python validate/score scripts can drive the B200 kernels directly:
+
+    st = tria_b200.load("stats.bin")                  # tria_load
+    out = tria_b200.score_kv_head(st, k_re, k_im, key_pos, cur_pos, layer, kvh)
+    ctx = tria_b200.Context(st, device=0)             # device path
+    ctx.evict(src_view, dst_view, n_rows, params, stream)
+
+There is no CPU fallback: if the shared library is missing this module
+raises on import of the library, and every device call reports the CUDA
+status it got.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libtriattention_b200.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "triattention.h")
+
+TYPE_F16 = 1
+TYPE_Q8_0 = 8
+
+OK = 0
+ERR_INVALID = -1
+ERR_CUDA = -2
+ERR_NOMEM = -3
+ERR_POSITION = -4
+ERR_UNSUPPORTED = -5
+ERR_NO_DEVICE = -6
+
+
+class TriaError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"[{status}] {msg}")
+        self.status = status
+
+
+class HeadStats(C.Structure):
+    _fields_ = [("q_mean_real", C.POINTER(C.c_float)), ("q_mean_imag", C.POINTER(C.c_float)),
+                ("q_abs_mean", C.POINTER(C.c_float)), ("qma", C.POINTER(C.c_float))]
+
+
+class Stats(C.Structure):
+    """struct tria_stats (triattention.h:38-50 of the reference)."""
+    _fields_ = [("num_layers", C.c_uint32), ("num_heads", C.c_uint32), ("num_kv_heads", C.c_uint32),
+                ("head_dim", C.c_uint32), ("freq_count", C.c_uint32), ("rope_theta", C.c_float),
+                ("attn_scale", C.c_float), ("layer_budget_scales", C.POINTER(C.c_float)),
+                ("omega", C.POINTER(C.c_float)), ("heads", C.POINTER(HeadStats))]
+
+
+class KvView(C.Structure):
+    """struct tria_kv_view."""
+    _fields_ = [("type", C.c_int32), ("n_layer", C.c_int32), ("layer0", C.c_int32),
+                ("n_head_kv", C.c_int32), ("head0", C.c_int32), ("n_cells", C.c_int32),
+                ("cell_stride", C.c_int64), ("head_stride", C.c_int64),
+                ("k", C.POINTER(C.c_void_p)), ("v", C.POINTER(C.c_void_p)),
+                ("pos", C.c_void_p), ("pos_shared", C.c_int32), ("reserved", C.c_int32)]
+
+
+class EvictParams(C.Structure):
+    """struct tria_evict_params."""
+    _fields_ = [("cur_pos", C.c_int32), ("budget", C.c_int32), ("ramp_pct", C.c_int32),
+                ("window", C.c_int32), ("sink", C.c_int32), ("reserved", C.c_int32)]
+
+
+def build() -> str:
+    """Compile the library in-tree (nvcc, sm_100a)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is not built; run `make -C {HERE}`")
+        L = C.CDLL(LIB_PATH)
+        L.tria_load.restype = C.POINTER(Stats)
+        L.tria_load.argtypes = [C.c_char_p]
+        L.tria_free.argtypes = [C.POINTER(Stats)]
+        L.tria_score_kv_head.argtypes = [C.POINTER(Stats), C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]
+        L.tria_status_str.restype = C.c_char_p
+        L.tria_status_str.argtypes = [C.c_int]
+        L.tria_last_error.restype = C.c_char_p
+        L.tria_ctx_create.argtypes = [C.POINTER(Stats), C.c_int, C.POINTER(C.c_void_p)]
+        L.tria_ctx_destroy.argtypes = [C.c_void_p]
+        L.tria_score.argtypes = [C.c_void_p, C.POINTER(KvView), C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]
+        L.tria_select.argtypes = [C.c_void_p, C.POINTER(KvView), C.c_void_p, C.c_void_p,
+                                  C.POINTER(EvictParams), C.c_void_p, C.c_void_p, C.c_void_p]
+        L.tria_compact.argtypes = [C.c_void_p, C.POINTER(KvView), C.POINTER(KvView), C.c_void_p,
+                                   C.c_void_p, C.c_void_p, C.c_void_p]
+        L.tria_evict.argtypes = [C.c_void_p, C.POINTER(KvView), C.POINTER(KvView), C.c_void_p,
+                                 C.POINTER(EvictParams), C.c_void_p, C.c_void_p]
+        L.tria_get_n_kv.argtypes = [C.c_void_p, C.c_void_p, C.c_int32]
+        L.tria_ctx_set_timing.argtypes = [C.c_void_p, C.c_int]
+        L.tria_ctx_stage_ms.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+        L.tria_ctx_launches.restype = C.c_int64
+        L.tria_ctx_launches.argtypes = [C.c_void_p]
+        L.tria_score_kv_head_dev.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
+                                             C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]
+        _lib = L
+    return _lib
+
+
+def exported_symbols_in_header(path: str = HEADER):
+    """Names of every function the header declares with TRIA_API."""
+    txt = open(path).read()
+    return sorted(set(re.findall(r"TRIA_API\s+[^;(]*?\b(tria_\w+)\s*\(", txt)))
+
+
+def last_error() -> str:
+    return lib().tria_last_error().decode()
+
+
+def check(status: int) -> None:
+    if status != OK:
+        raise TriaError(status, f"{lib().tria_status_str(status).decode()}: {last_error()}")
+
+
+# ---------------- reference API ----------------
+
+def load(path: str):
+    """tria_load: returns a ctypes pointer to Stats (falsy on failure)."""
+    p = lib().tria_load(os.fsencode(path))
+    return p if p else None
+
+
+def free(stats) -> None:
+    if stats:
+        lib().tria_free(stats)
+
+
+def score_kv_head(stats, k_re, k_im, key_pos, cur_pos, layer, kv_head):
+    """tria_score_kv_head on host arrays (fp32 [n, fc] halves, int32 positions)."""
+    k_re = np.ascontiguousarray(k_re, np.float32)
+    k_im = np.ascontiguousarray(k_im, np.float32)
+    key_pos = np.ascontiguousarray(key_pos, np.int32)
+    n = int(key_pos.shape[0])
+    out = np.empty(max(n, 1), np.float32)
+    lib().tria_score_kv_head(stats, k_re.ctypes.data, k_im.ctypes.data, key_pos.ctypes.data,
+                             int(cur_pos), n, int(layer), int(kv_head), out.ctypes.data)
+    return out[:n]
+
+
+def layer_budget(stats, layer, base_budget):
+    """tria_layer_budget (the header's static inline, restated for Python)."""
+    scale = np.float32(stats.contents.layer_budget_scales[layer])
+    b = int(np.float32(np.float32(base_budget) * scale))
+    return b if b > 0 else 1
+
+
+# ---------------- device path ----------------
+
+def _ptr(x) -> int:
+    """Device pointer of a torch tensor or an int."""
+    if x is None:
+        return 0
+    if isinstance(x, int):
+        return x
+    return int(x.data_ptr())
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        return 0
+    if isinstance(stream, int):
+        return stream
+    return int(stream.cuda_stream)
+
+
+def make_view(type_id, k_layers, v_layers, pos, n_cells, cell_stride, head_stride,
+              n_head_kv, layer0=0, head0=0, pos_shared=False):
+    """Build a KvView; k_layers / v_layers are lists of torch tensors or device pointers.
+    The returned view keeps its pointer arrays alive."""
+    nl = len(k_layers)
+    karr = (C.c_void_p * nl)(*[_ptr(t) for t in k_layers])
+    varr = (C.c_void_p * nl)(*[_ptr(t) for t in v_layers]) if v_layers is not None else None
+    v = KvView(type_id, nl, layer0, n_head_kv, head0, n_cells, cell_stride, head_stride,
+               C.cast(karr, C.POINTER(C.c_void_p)),
+               C.cast(varr, C.POINTER(C.c_void_p)) if varr is not None else None,
+               _ptr(pos), 1 if pos_shared else 0, 0)
+    v._keep = (karr, varr, k_layers, v_layers, pos)
+    return v
+
+
+class Context:
+    def __init__(self, stats, device: int = 0):
+        h = C.c_void_p()
+        check(lib().tria_ctx_create(stats, device, C.byref(h)))
+        self.h = h
+        self.stats = stats
+
+    def close(self):
+        if self.h:
+            lib().tria_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @staticmethod
+    def _rows(n_rows):
+        a = np.ascontiguousarray(n_rows, np.int32)
+        return a, a.ctypes.data
+
+    def score(self, view, n_rows, cur_pos, scores, stream=None):
+        a, p = self._rows(n_rows)
+        check(lib().tria_score(self.h, C.byref(view), p, int(cur_pos), _ptr(scores), _stream(stream)))
+
+    def select(self, view, n_rows, scores, params, kept_idx, n_kept, stream=None):
+        a, p = self._rows(n_rows)
+        check(lib().tria_select(self.h, C.byref(view), p, _ptr(scores), C.byref(params),
+                                _ptr(kept_idx), _ptr(n_kept), _stream(stream)))
+
+    def compact(self, src, dst, n_rows, kept_idx, n_kept, stream=None):
+        a, p = self._rows(n_rows)
+        check(lib().tria_compact(self.h, C.byref(src), C.byref(dst), p, _ptr(kept_idx),
+                                 _ptr(n_kept), _stream(stream)))
+
+    def evict(self, src, dst, n_rows, params, n_kept_out=None, stream=None):
+        a, p = self._rows(n_rows)
+        check(lib().tria_evict(self.h, C.byref(src), C.byref(dst), p, C.byref(params),
+                               _ptr(n_kept_out), _stream(stream)))
+
+    def get_n_kv(self, units: int = 0):
+        buf = np.zeros(max(units, 1), np.int32)
+        r = lib().tria_get_n_kv(self.h, buf.ctypes.data if units else None, units)
+        if r < 0:
+            check(r)
+        return r, buf[:units]
+
+    def set_timing(self, on: bool = True):
+        check(lib().tria_ctx_set_timing(self.h, 1 if on else 0))
+
+    STAGES = ("table", "score", "znorm", "select", "compact")
+
+    def stage_ms(self):
+        """Device ms per stage of the last timed evict: dict stage -> ms."""
+        buf = np.zeros(5, np.float32)
+        k = lib().tria_ctx_stage_ms(self.h, buf.ctypes.data, 5)
+        if k < 0:
+            check(k)
+        return {n: float(buf[i]) for i, n in enumerate(self.STAGES[:k])}
+
+    def launches(self) -> int:
+        return int(lib().tria_ctx_launches(self.h))
+
+    def score_kv_head_dev(self, k_re, k_im, key_pos, cur_pos, n, layer, kv_head, out, stream=None):
+        check(lib().tria_score_kv_head_dev(self.h, _ptr(k_re), _ptr(k_im), _ptr(key_pos), int(cur_pos),
+                                           int(n), int(layer), int(kv_head), _ptr(out), _stream(stream)))
