@@ -160,7 +160,7 @@ struct tria_evict_params {
     int32_t cur_pos;     /* trigger (decode) position; every key position must be <= cur_pos */
     int32_t budget;      /* base budget in rows per (layer, kv-head), before the layer scale */
     int32_t ramp_pct;    /* 0..100 */
-    int32_t window;      /* rows with cur_pos - pos < window are always kept (0 = none) */
+    int32_t window;      /* rows with pos >= cur_pos - window are always kept (0 = none) */
     int32_t sink;        /* rows with pos < sink are always kept (0 = none) */
     int32_t reserved;
 };

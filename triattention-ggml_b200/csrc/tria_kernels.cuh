@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(SELECT_THREADS) k_select(const SelectArgs a) {
         uint32_t k = score_key(x);
         if (prot_on) {
             const int p = a.pos[a.pos_shared ? (int64_t)r : (int64_t)u * a.pos_cells + r];
-            if ((a.sink > 0 && p < a.sink) || (a.window > 0 && a.cur_pos - p < a.window)) {
+            if ((a.sink > 0 && p < a.sink) || (a.window > 0 && p >= a.cur_pos - a.window)) {
                 k = 0xffffffffu;
                 prot++;
             }
