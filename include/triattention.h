@@ -230,6 +230,40 @@ TRIA_API int tria_score_kv_head_dev(tria_ctx *ctx, const float *k_re, const floa
                                     const int32_t *key_pos, int32_t cur_pos, int32_t n,
                                     int32_t layer, int32_t kv_head, float *out, void *stream);
 
+/* Maximum number of scores tria_select_noalloc can rank in one call
+ * (sum over units of the per-unit row capacity, see below): 1 Mi keys, 4 MiB. */
+#define TRIA_NOALLOC_MAX_KEYS (1 << 20)
+
+/* Selection that allocates no memory at all.  No counterpart in the
+ * reference: it exists for callers that must not allocate device memory at
+ * the time they evict, such as a runtime whose memory pool owns the whole
+ * GPU, code running inside a CUDA graph capture or a memory-planned inference
+ * graph, or plugins whose host forbids cudaMalloc.  It ranks `scores` exactly
+ * like tria_select (order-preserving keys, best `keep[u]` rows of each unit by
+ * (score desc, row asc), protected window/sink rows first) but takes the kept
+ * counts directly, needs no context, and keeps its 32-bit sort keys in one
+ * static device array of TRIA_NOALLOC_MAX_KEYS entries that every GPU loading
+ * this library holds until the process exits.
+ *   scores    device, [units][score_stride] fp32
+ *   n_rows    host, [units] rows per unit (each <= score_stride, kept_stride)
+ *   keep      host, [units] rows to keep (clamped to [protected rows, n_rows])
+ *   pos       device positions, [units][pos_stride] or one shared [rows] array
+ *             when pos_stride == 0; may be NULL when window == sink == 0
+ *   kept_idx  device, [units][kept_stride] kept row indices, ascending
+ *   n_kept    device, [units] kept counts
+ * units * (max n_rows rounded up to 64) must not exceed TRIA_NOALLOC_MAX_KEYS
+ * (TRIA_ERR_UNSUPPORTED otherwise, nothing launched).  Runs on the current
+ * device; the first call on a device looks the array's address up
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * All calls share the one array: calls that overlap on the GPU (different
+ * streams, or different host threads) race and corrupt each other's result. */
+TRIA_API int tria_select_noalloc(const float *scores, int64_t score_stride,
+                                 const int32_t *n_rows, const int32_t *keep, int32_t units,
+                                 const int32_t *pos, int64_t pos_stride,
+                                 int32_t cur_pos, int32_t window, int32_t sink,
+                                 int32_t *kept_idx, int64_t kept_stride, int32_t *n_kept,
+                                 void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -869,3 +869,83 @@ extern "C" TRIA_API void tria_score_kv_head(const tria_stats *stats, const float
             for (int r = 0; r < seq_len; r++) out_scores[r] = NAN;
     }
 }
+
+/* ------------------------------------------------------------------ */
+/* Selection without allocation                                         */
+/* ------------------------------------------------------------------ */
+
+/* Sort keys of tria_select_noalloc.  Every device that loads this library
+ * holds these 4 MiB until exit; nothing in it has to start at zero (each call
+ * writes every key it reads). */
+static __device__ __align__(256) uint32_t g_noalloc_keys[TRIA_NOALLOC_MAX_KEYS];
+
+static std::mutex g_noalloc_mu;
+static uint32_t *g_noalloc_ptr[256];   /* device address of g_noalloc_keys, per device */
+
+/* Device address of the static key array on the current device, looked up
+ * once per device (host code cannot use the symbol itself as a pointer). */
+static int noalloc_keys(uint32_t **out) {
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 256) FAIL(TRIA_ERR_UNSUPPORTED, "device index %d too large", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        int rc = check_device(dev);
+        if (rc) return rc;
+        void *p = nullptr;
+        CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_keys));
+        g_noalloc_ptr[dev] = (uint32_t *)p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return TRIA_OK;
+}
+
+extern "C" TRIA_API int tria_select_noalloc(const float *scores, int64_t score_stride, const int32_t *n_rows,
+                                            const int32_t *keep, int32_t units, const int32_t *pos,
+                                            int64_t pos_stride, int32_t cur_pos, int32_t window, int32_t sink,
+                                            int32_t *kept_idx, int64_t kept_stride, int32_t *n_kept,
+                                            void *stream) {
+    if (!scores || !n_rows || !keep || !kept_idx || !n_kept)
+        FAIL(TRIA_ERR_INVALID, "tria_select_noalloc: null argument");
+    if (units < 1 || units > TRIA_MAX_UNITS)
+        FAIL(TRIA_ERR_INVALID, "tria_select_noalloc: units %d outside [1, %d]", units, TRIA_MAX_UNITS);
+    if ((window > 0 || sink > 0) && !pos)
+        FAIL(TRIA_ERR_INVALID, "tria_select_noalloc: window/sink need positions");
+    int32_t max_rows = 0;
+    for (int u = 0; u < units; u++) {
+        if (n_rows[u] < 0 || n_rows[u] > score_stride || n_rows[u] > kept_stride ||
+            (pos && pos_stride > 0 && n_rows[u] > pos_stride))
+            FAIL(TRIA_ERR_INVALID, "tria_select_noalloc: n_rows[%d] = %d exceeds a stride", u, n_rows[u]);
+        max_rows = std::max(max_rows, n_rows[u]);
+    }
+    const int64_t key_stride = ((int64_t)max_rows + 63) & ~(int64_t)63;
+    if ((int64_t)units * key_stride > TRIA_NOALLOC_MAX_KEYS)
+        FAIL(TRIA_ERR_UNSUPPORTED,
+             "tria_select_noalloc: %d units x %lld rows exceed the fixed scratch of %d keys; "
+             "use tria_select or fewer units per call", units, (long long)key_stride, TRIA_NOALLOC_MAX_KEYS);
+    uint32_t *keys = nullptr;
+    int rc = noalloc_keys(&keys);
+    if (rc) return rc;
+    SelectArgs a;                       /* passed by value: no allocation */
+    memset(&a, 0, sizeof a);
+    a.scores = scores;
+    a.score_stride = score_stride;
+    a.pos = pos;
+    a.pos_shared = pos_stride == 0 ? 1 : 0;
+    a.pos_cells = (int32_t)pos_stride;
+    a.cur_pos = cur_pos;
+    a.window = window;
+    a.sink = sink;
+    a.keys = keys;
+    a.key_stride = key_stride;
+    a.kept_idx = kept_idx;
+    a.kept_stride = kept_stride;
+    a.n_kept = n_kept;
+    for (int u = 0; u < units; u++) {
+        a.n_rows[u] = n_rows[u];
+        a.keep_req[u] = keep[u];
+    }
+    k_select<false><<<units, SELECT_THREADS, 0, (cudaStream_t)stream>>>(a);
+    CUDA_TRY(cudaGetLastError());
+    return TRIA_OK;
+}

@@ -109,6 +109,9 @@ def lib() -> C.CDLL:
         L.tria_ctx_stage_ms.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
         L.tria_ctx_launches.restype = C.c_int64
         L.tria_ctx_launches.argtypes = [C.c_void_p]
+        L.tria_select_noalloc.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int32,
+                                          C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
+                                          C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]
         L.tria_score_kv_head_dev.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
                                              C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]
         _lib = L
@@ -163,6 +166,21 @@ def layer_budget(stats, layer, base_budget):
 
 
 # ---------------- device path ----------------
+
+NOALLOC_MAX_KEYS = 1 << 20
+
+
+def select_noalloc(scores, score_stride, n_rows, keep, kept_idx, kept_stride, n_kept,
+                   pos=None, pos_stride=0, cur_pos=0, window=0, sink=0, stream=None):
+    """tria_select_noalloc: rank device scores with no allocation (fixed static
+    scratch of NOALLOC_MAX_KEYS keys; see the header)."""
+    nr = np.ascontiguousarray(n_rows, np.int32)
+    kp = np.ascontiguousarray(keep, np.int32)
+    assert nr.shape == kp.shape
+    check(lib().tria_select_noalloc(_ptr(scores), int(score_stride), nr.ctypes.data, kp.ctypes.data,
+                                    int(nr.shape[0]), _ptr(pos), int(pos_stride), int(cur_pos),
+                                    int(window), int(sink), _ptr(kept_idx), int(kept_stride),
+                                    _ptr(n_kept), _stream(stream)))
 
 def _ptr(x) -> int:
     """Device pointer of a torch tensor or an int."""
