@@ -446,10 +446,14 @@ def main():
     ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profile a smaller case: only the first N layers of the workload")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.layers:
+        CONFIGS[args.config] = dict(CONFIGS[args.config], L=args.layers)
     if args.impl == "reference":
         run_reference(args)
     else:

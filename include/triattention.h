@@ -212,6 +212,14 @@ TRIA_API int tria_evict(tria_ctx *ctx, const struct tria_kv_view *src,
  * keep (README.md:92, "max over sequences").  Negative on error. */
 TRIA_API int tria_get_n_kv(tria_ctx *ctx, int32_t *n_kept, int32_t cap);
 
+/* Z-norm statistics of `chains` score arrays, bit-identical to the
+ * reference's sequential fp32 mean and population std (triattention.c:227-238,
+ * std clamped at 1e-6): x device [chains][stride] fp32 (16-byte aligned,
+ * stride % 4 == 0), n host [chains] rows, mean_std device [chains][2]
+ * (mean, std).  Needs no context.  New: stage 3 of the step on its own. */
+TRIA_API int tria_znorm_stats(const float *x, int64_t stride, const int32_t *n, int32_t chains,
+                              float *mean_std, void *stream);
+
 /* Stage timing of the following tria_evict calls on `ctx` (off by default):
  * CUDA events are recorded on the call's stream between the stages. */
 TRIA_API int tria_ctx_set_timing(tria_ctx *ctx, int enable);

@@ -163,11 +163,14 @@ def _oracle_unit_scores(oracle, ost, type_id, K, pos, l, h, n, hd, cur_pos, laye
     return oracle.score_kv_head(ost, re, im, pos[l, h, :n], cur_pos, layer0 + l, head0 + h)
 
 
-@pytest.mark.parametrize("type_id,shared", [(workloads.TYPE_F16, True), (workloads.TYPE_F16, False),
-                                            (workloads.TYPE_Q8_0, True), (workloads.TYPE_Q8_0, False)])
-def test_tria_score_cache_vs_oracle(torch_dev, oracle, tmp_path_factory, type_id, shared):
+@pytest.mark.parametrize("type_id,shared,n_cells", [
+    (workloads.TYPE_F16, True, 2600), (workloads.TYPE_F16, False, 2600),
+    (workloads.TYPE_Q8_0, True, 2600), (workloads.TYPE_Q8_0, False, 2600),
+    (workloads.TYPE_F16, False, 2601),          # n_cells % 4 != 0: the general scoring kernel
+])
+def test_tria_score_cache_vs_oracle(torch_dev, oracle, tmp_path_factory, type_id, shared, n_cells):
     import torch
-    L, H, KV, hd, n_cells, cur = 3, 32, 8, 128, 2600, 4000
+    L, H, KV, hd, cur = 3, 32, 8, 128, 4000
     path = _stats_file(tmp_path_factory, "c.tria", L, H, KV, hd, 1e6, seed=11)
     st, ost = tria_b200.load(path), oracle.load(path)
     try:

@@ -391,9 +391,11 @@ static int launch_znorm(tria_ctx *c, int64_t unit0, int units, const int32_t *n_
     z.G = (int32_t)c->G;
     z.units = units;
     z.ms = c->ms + unit0 * c->G;
+    z.csum = nullptr;
+    z.n_chunks = 0;
     for (int u = 0; u < units; u++) z.n_rows[u] = n_rows[unit0 + u];
     const int chains = units * (int)c->G;
-    k_znorm_seq<<<(chains + 31) / 32, 32, 0, st>>>(z);
+    k_znorm_exact<<<chains, ZN_THREADS, 0, st>>>(z);
     CUDA_TRY(cudaGetLastError());
     c->launches++;
     return TRIA_OK;
@@ -481,8 +483,11 @@ static int launch_select(tria_ctx *c, const tria_kv_view *v, const int32_t *n_ro
     });
 }
 
+/* rows_hint: expected kept rows per unit, only sizes the grid (the kernel is
+ * grid-stride, so any count on the device is copied whatever the hint). */
 static int launch_compact(tria_ctx *c, const tria_kv_view *s, const tria_kv_view *d, const int32_t *n_rows,
-                          const int32_t *kept_idx, int64_t kept_stride, const int32_t *n_kept, cudaStream_t st) {
+                          const int32_t *kept_idx, int64_t kept_stride, const int32_t *n_kept, cudaStream_t st,
+                          int rows_hint = -1) {
     const int64_t rb = view_row_bytes(s->type, (int)c->hd);
     auto al = [](int64_t x) { return x & 15 ? (x & 7 ? 4 : 8) : 16; };
     int vec = std::min({al(rb), al(s->cell_stride), al(s->head_stride), al(d->cell_stride), al(d->head_stride)});
@@ -512,7 +517,8 @@ static int launch_compact(tria_ctx *c, const tria_kv_view *s, const tria_kv_view
         a->has_v = s->v ? 1 : 0;
         int max_rows = 0;
         for (int u = 0; u < units; u++) max_rows = std::max(max_rows, n_rows[u0 + u]);
-        const int64_t work = (int64_t)max_rows * (rb / vec);
+        const int rows = rows_hint >= 0 ? std::min(rows_hint, max_rows) : max_rows;
+        const int64_t work = (int64_t)std::max(rows, 1) * (rb / vec);
         const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 1024));
         dim3 grid(gx, units);
         if (max_rows > 0) {
@@ -635,7 +641,10 @@ extern "C" TRIA_API int tria_evict(tria_ctx *c, const tria_kv_view *s, const tri
     if ((rc = stage(3))) return rc;
     if ((rc = launch_select(c, s, n_rows, keep, p, true, nullptr, c->kept, c->cell_stride, cnt, st))) return rc;
     if ((rc = stage(4))) return rc;
-    if ((rc = launch_compact(c, s, d, n_rows, c->kept, c->cell_stride, cnt, st))) return rc;
+    int hint = 0;
+    for (int32_t k : keep) hint = std::max(hint, k);
+    if (p->window > 0 || p->sink > 0) hint += std::max(0, p->window) + std::max(0, p->sink) + 1;
+    if ((rc = launch_compact(c, s, d, n_rows, c->kept, c->cell_stride, cnt, st, hint))) return rc;
     if ((rc = stage(5))) return rc;
     c->have_timing = c->timing;
     CUDA_TRY(cudaMemcpyAsync(c->h_pinned, c->d_status, 4, cudaMemcpyDeviceToHost, st));
@@ -662,6 +671,29 @@ extern "C" TRIA_API int tria_get_n_kv(tria_ctx *c, int32_t *n_kept, int32_t cap)
         if (n_kept && u < cap) n_kept[u] = c->h_pinned[1 + u];
     }
     return mx;
+}
+
+extern "C" TRIA_API int tria_znorm_stats(const float *x, int64_t stride, const int32_t *n, int32_t chains,
+                                         float *mean_std, void *stream) {
+    if (!x || !n || !mean_std || chains < 0) FAIL(TRIA_ERR_INVALID, "tria_znorm_stats: bad argument");
+    if (((uintptr_t)x & 15) || (stride & 3)) FAIL(TRIA_ERR_INVALID, "tria_znorm_stats: x must be 16-byte aligned, stride % 4 == 0");
+    for (int i = 0; i < chains; i++)
+        if (n[i] < 0 || n[i] > stride) FAIL(TRIA_ERR_INVALID, "tria_znorm_stats: n[%d] = %d outside [0, stride]", i, n[i]);
+    for (int c0 = 0; c0 < chains; c0 += TRIA_MAX_UNITS) {
+        const int cn = std::min(TRIA_MAX_UNITS, chains - c0);
+        ZArgs z;
+        z.raw = x + (int64_t)c0 * stride;
+        z.raw_stride = stride;
+        z.G = 1;
+        z.units = cn;
+        z.ms = reinterpret_cast<float2 *>(mean_std) + c0;
+        z.csum = nullptr;
+        z.n_chunks = 0;
+        for (int i = 0; i < cn; i++) z.n_rows[i] = n[c0 + i];
+        k_znorm_exact<<<cn, ZN_THREADS, 0, (cudaStream_t)stream>>>(z);
+        CUDA_TRY(cudaGetLastError());
+    }
+    return TRIA_OK;
 }
 
 extern "C" TRIA_API int tria_ctx_set_timing(tria_ctx *c, int enable) {

@@ -18,8 +18,9 @@
  *                     raw_g = (sum_f qr_gf X_f + qi_gf Y_f) / 17 + sum_f res_gf |k_f|
  *                  which is triattention.c:156-192 with the offset sum moved
  *                  into the table (rel_r cos - rel_i sin summed over o).
- *   k_znorm_seq    mean and variance as the reference's sequential fp32 chains
- *                  (triattention.c:228-236), IEEE div/sqrt, std clamp 1e-6.
+ *   k_znorm_exact  mean and variance bit-identical to the reference's
+ *                  sequential fp32 chains (triattention.c:228-236), computed
+ *                  as chunked ulp-grid translations; IEEE div/sqrt, clamp 1e-6.
  *   k_select       z-score max over the group (triattention.c:240-247), an
  *                  order-preserving 32-bit key, 8-bit radix select of the
  *                  keep-th largest key, ties to the lowest rows, and an
@@ -34,6 +35,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <climits>
 
 #include "tria_internal.h"
 
@@ -230,50 +232,313 @@ __global__ void __launch_bounds__(SCORE_THREADS) k_score_raw(const ScoreArgs a) 
 }
 
 /* ------------------------------------------------------------------ */
-/* Z-norm statistics: sequential fp32, triattention.c:228-238          */
+/* Z-norm statistics: the reference's sequential fp32 chains, exactly    */
 /* ------------------------------------------------------------------ */
+/*
+ * triattention.c:228-236 forms mean = fl(sum)/n and var with two sequential
+ * fp32 chains  s <- fl(s + v_k).  Summing more accurately would move z by up
+ * to ~1e-5 at 32k rows, so the chains are reproduced bit for bit, but in
+ * parallel:
+ *
+ * While s and every partial result stay in one binade [2^E, 2^(E+1)), each
+ * fp32 add rounds on the fixed grid ulp = 2^(E-23): with s = M*ulp (M the
+ * 24-bit significand), fl(s + v) = (M + round(v/ulp))*ulp, ties to even M.
+ * So a chunk of adds is an integer translation D of M that depends only on E
+ * and on the parity of M (ties).  The CTA predicts E for every chunk from a
+ * double prefix sum, builds (D_end, D_min, D_max) per chunk and per parity
+ * (phase B, a warp per chunk), then warp 0 walks the chunks (phase C): it
+ * applies a chunk's translation only when the running s is really in the
+ * predicted binade and M + D stays strictly inside [2^23, 2^24) for every
+ * partial sum -- which proves each exact s_k + v_k was inside the binade, so
+ * the grid rounding was the fp32 rounding.  Any other chunk (the first ones,
+ * binade crossings, NaN/Inf, huge values) is added the sequential way.  The
+ * result is identical to the reference's chain for every input; the
+ * prediction only decides how many chunks take the slow path.
+ */
+
+constexpr int ZN_THREADS = 128;
+constexpr int ZN_MAXCH = 512;          /* chunks per chain kept in shared memory */
+constexpr int ZN_CHUNK_ROWS = 128;     /* rows per predictor sum written by the scoring kernel */
 
 struct ZArgs {
     const float *raw;
     int64_t raw_stride;
     int32_t G, units;
     float2 *ms;                          /* [units*G] (mean, std) */
+    const double *csum;                  /* optional [units*G][n_chunks][2] per-128-row (sum, sum sq) */
+    int32_t n_chunks;
     int32_t n_rows[TRIA_MAX_UNITS];
 };
 
-__global__ void k_znorm_seq(const ZArgs a) {
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+struct ZnShared {
+    double P[ZN_MAXCH];                  /* chunk sums, then prefix sums at chunk starts */
+    int dend[2][ZN_MAXCH], dmin[2][ZN_MAXCH], dmax[2][ZN_MAXCH];
+    short E[ZN_MAXCH];
+    unsigned char ok[ZN_MAXCH];
+    double wsum[ZN_THREADS / 32];
+    float stage[128];                    /* one 128-element piece of a fallback chunk */
+    float result;
+};
+
+/* v/ulp rounded onto the integer grid of binade E (ulp = 2^(E-23)), given the
+ * parity of the running significand.  Returns 0 = ok, 1 = tie (d assumes the
+ * given parity), 2 = v cannot stay within the binade (or is not finite). */
+__device__ __forceinline__ int grid_delta(float v, int E, int par, int &d) {
+    const uint32_t b = __float_as_uint(v);
+    const int exb = (b >> 23) & 0xff;
+    if (exb == 255) return 2;
+    const int m24 = exb ? (int)((b & 0x7fffffu) | 0x800000u) : (int)(b & 0x7fffffu);
+    const int ex = exb ? exb - 127 : -126;
+    const int sh = E - ex;                              /* v/ulp = +-m24 * 2^-sh */
+    if (sh < 0) return 2;
+    const int Q = (b >> 31) ? -m24 : m24;
+    if (sh == 0) { d = Q; return (Q >= (1 << 23) || Q <= -(1 << 23)) ? 2 : 0; }
+    if (sh >= 25) { d = 0; return 0; }                  /* |v/ulp| < 1/2 */
+    const int fl = Q >> sh;                             /* floor */
+    const int r = Q & ((1 << sh) - 1);
+    const int half = 1 << (sh - 1);
+    if (r < half) { d = fl; return 0; }
+    if (r > half) { d = fl + 1; return 0; }
+    d = ((par + fl) & 1) ? fl + 1 : fl;                 /* tie: even significand */
+    return 1;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int m = 16; m; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    return v;
+}
+
+/* Four consecutive elements [k, k+4) of x (k % 4 == 0); `cnt` of them exist. */
+__device__ __forceinline__ float4 load4(const float *__restrict__ x, int k, int n, int &cnt) {
+    cnt = max(0, min(4, n - k));
+    if (cnt == 4) return __ldcg(reinterpret_cast<const float4 *>(x + k));
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (cnt > 0) v.x = x[k];
+    if (cnt > 1) v.y = x[k + 1];
+    if (cnt > 2) v.z = x[k + 2];
+    return v;
+}
+
+/* The fp32 sequential sum of val(x[0..n)) (val = identity for the mean, the
+ * reference's fl(fl(x-mean)^2) for the variance).  x is 16-byte aligned; a
+ * chunk is M = 128*P elements, P pieces of one float4 per lane.  When
+ * have_sums, sh.P already holds the chunk sums (they only steer the binade
+ * guess).  Result valid in all threads. */
+template <class Val>
+__device__ float exact_chain_sum(const float *__restrict__ x, int n, int M, int nch, ZnShared &sh, Val val,
+                                 bool have_sums) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = ZN_THREADS / 32;
+    const int P = M / 128;
+
+    /* A: chunk sums in double */
+    for (int j = have_sums ? nch : warp; j < nch; j += NW) {
+        const int b = j * M;
+        double acc = 0.0;
+        for (int pc = 0; pc < P; pc++) {
+            int c;
+            const float4 v = load4(x, b + 128 * pc + 4 * lane, n, c);
+            if (c > 0) acc += (double)val(v.x);
+            if (c > 1) acc += (double)val(v.y);
+            if (c > 2) acc += (double)val(v.z);
+            if (c > 3) acc += (double)val(v.w);
+        }
+        acc = warp_sum_d(acc);
+        if (lane == 0) sh.P[j] = acc;
+    }
+    __syncthreads();
+    {   /* exclusive prefix in chunk order */
+        const int cpt = (nch + ZN_THREADS - 1) / ZN_THREADS;
+        const int j0 = min(tid * cpt, nch), j1 = min(j0 + cpt, nch);
+        double loc = 0.0;
+        for (int j = j0; j < j1; j++) loc += sh.P[j];
+        double inc = loc;
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) {
+            const double t = __shfl_up_sync(0xffffffffu, inc, m);
+            if (lane >= m) inc += t;
+        }
+        if (lane == 31) sh.wsum[warp] = inc;
+        __syncthreads();
+        double base = inc - loc;
+        for (int w = 0; w < warp; w++) base += sh.wsum[w];
+        for (int j = j0; j < j1; j++) { const double t = sh.P[j]; sh.P[j] = base; base += t; }
+    }
+    __syncthreads();
+
+    /* B: per-chunk translations (a warp per chunk, pieces in element order) */
+    for (int j = warp; j < nch; j += NW) {
+        const int b = j * M, e = min(b + M, n);
+        const double pj = sh.P[j];
+        int E = 0;
+        bool valid = false;
+        if (pj != 0.0) {
+            const int exd = (__double2hiint(pj) >> 20) & 0x7ff;
+            E = exd - 1023;
+            valid = exd != 0x7ff && E >= -126 && E <= 127;
+        }
+        if (!valid) { if (lane == 0) sh.ok[j] = 0; continue; }
+        int run = 0, gmin = INT_MAX, gmax = INT_MIN;
+        bool bad = false, tie = false;
+        for (int pc = 0; pc < P; pc++) {
+            int c0;
+            const float4 v0 = load4(x, b + 128 * pc + 4 * lane, n, c0);
+            const float vv[4] = {v0.x, v0.y, v0.z, v0.w};
+            int dsum = 0, lmin = INT_MAX, lmax = INT_MIN;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                if (t < c0) {
+                    int d = 0;
+                    const int st = grid_delta(val(vv[t]), E, 0, d);
+                    bad |= st == 2;
+                    tie |= st == 1;
+                    dsum += d;
+                    lmin = min(lmin, dsum);
+                    lmax = max(lmax, dsum);
+                }
+            }
+            if (dsum > (1 << 23) || dsum < -(1 << 23)) bad = true;
+            int inc = dsum;
+#pragma unroll
+            for (int m = 1; m < 32; m <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, inc, m);
+                if (lane >= m) inc += t;
+            }
+            const int off = run + inc - dsum;
+            if (lmin != INT_MAX) { gmin = min(gmin, lmin + off); gmax = max(gmax, lmax + off); }
+            run += __shfl_sync(0xffffffffu, inc, 31);
+            if (run > (1 << 23) || run < -(1 << 23)) bad = true;
+        }
+        if (__any_sync(0xffffffffu, bad)) { if (lane == 0) sh.ok[j] = 0; continue; }
+        if (!__any_sync(0xffffffffu, tie)) {
+#pragma unroll
+            for (int m = 16; m; m >>= 1) {
+                gmin = min(gmin, __shfl_xor_sync(0xffffffffu, gmin, m));
+                gmax = max(gmax, __shfl_xor_sync(0xffffffffu, gmax, m));
+            }
+            if (lane == 0) {
+                const bool fits = gmin >= -(1 << 23) && gmax <= (1 << 23);
+                for (int p = 0; p < 2; p++) { sh.dend[p][j] = run; sh.dmin[p][j] = gmin; sh.dmax[p][j] = gmax; }
+                sh.E[j] = (short)E;
+                sh.ok[j] = fits ? 1 : 0;
+            }
+        } else if (lane == 0) {                          /* ties: the parity path matters */
+            bool fits = true;
+            for (int p = 0; p < 2 && fits; p++) {
+                int D = 0, mn = INT_MAX, mx = INT_MIN;
+                for (int k = b; k < e && fits; k++) {
+                    int d = 0;
+                    if (grid_delta(val(x[k]), E, (p + D) & 1, d) == 2) fits = false;
+                    D += d;
+                    mn = min(mn, D);
+                    mx = max(mx, D);
+                    if (D > (1 << 23) || D < -(1 << 23)) fits = false;
+                }
+                sh.dend[p][j] = D; sh.dmin[p][j] = mn; sh.dmax[p][j] = mx;
+            }
+            sh.E[j] = (short)E;
+            sh.ok[j] = fits ? 1 : 0;
+        }
+    }
+    __syncthreads();
+
+    /* C: warp 0 walks the chunks (all lanes in step, same values); a chunk
+     * that cannot be translated is staged through shared memory, 128
+     * elements at a time, and added sequentially. */
+    if (warp == 0) {
+        float s = 0.f;
+        for (int j = 0; j < nch; j++) {
+            bool done = false;
+            if (sh.ok[j]) {
+                const uint32_t bits = __float_as_uint(s);
+                const int exb = (bits >> 23) & 0xff;
+                if (exb != 0 && exb != 255 && exb - 127 == sh.E[j]) {
+                    const int mabs = (int)((bits & 0x7fffffu) | 0x800000u);
+                    const int p = mabs & 1;
+                    const bool neg = bits >> 31;
+                    const int ms = neg ? -mabs : mabs;
+                    const int lo = ms + sh.dmin[p][j], hi = ms + sh.dmax[p][j];
+                    const bool in = neg ? (hi <= -((1 << 23) + 1) && lo >= -((1 << 24) - 1))
+                                        : (lo >= (1 << 23) + 1 && hi <= (1 << 24) - 1);
+                    if (in) {
+                        const int mn = ms + sh.dend[p][j];
+                        const uint32_t a = (uint32_t)(neg ? -mn : mn);
+                        s = __uint_as_float((bits & 0x80000000u) | ((uint32_t)exb << 23) | (a & 0x7fffffu));
+                        done = true;
+                    }
+                }
+            }
+            if (!done) {
+                const int b = j * M, e = min(b + M, n);
+                for (int pb = b; pb < e; pb += 128) {
+                    int c;
+                    const float4 v = load4(x, pb + 4 * lane, n, c);
+                    __syncwarp();
+                    if (c > 0) sh.stage[4 * lane] = v.x;
+                    if (c > 1) sh.stage[4 * lane + 1] = v.y;
+                    if (c > 2) sh.stage[4 * lane + 2] = v.z;
+                    if (c > 3) sh.stage[4 * lane + 3] = v.w;
+                    __syncwarp();
+                    const int cnt = min(128, e - pb);
+#pragma unroll 8
+                    for (int k = 0; k < cnt; k++) s = __fadd_rn(s, val(sh.stage[k]));
+                }
+            }
+        }
+        if (lane == 0) sh.result = s;
+    }
+    __syncthreads();
+    const float r = sh.result;
+    __syncthreads();
+    return r;
+}
+
+/* One CTA per (unit, query head) chain: (mean, std) of triattention.c:227-238. */
+__global__ void __launch_bounds__(ZN_THREADS) k_znorm_exact(const ZArgs a) {
+    __shared__ ZnShared sh;
+    const int t = blockIdx.x;
     if (t >= a.units * a.G) return;
     const int n = a.n_rows[t / a.G];
     const float *x = a.raw + (int64_t)t * a.raw_stride;
-    const float4 *x4 = reinterpret_cast<const float4 *>(x);
-    const int n4 = n >> 2;
-    float s = 0.f;
-#pragma unroll 8
-    for (int i = 0; i < n4; i++) {
-        const float4 v = x4[i];
-        s = __fadd_rn(s, v.x); s = __fadd_rn(s, v.y);
-        s = __fadd_rn(s, v.z); s = __fadd_rn(s, v.w);
+    int M = 128;
+    while ((n + M - 1) / M > ZN_MAXCH) M *= 2;
+    const int nch = (n + M - 1) / M;
+    /* predictor sums from the scoring kernel when it produced them */
+    const bool pre = a.csum != nullptr;
+    const double *cs = pre ? a.csum + (int64_t)t * a.n_chunks * 2 : nullptr;
+    const int per = M / ZN_CHUNK_ROWS;
+    if (pre) {
+        for (int j = threadIdx.x; j < nch; j += ZN_THREADS) {
+            double s1 = 0.0;
+            for (int i = j * per; i < min((j + 1) * per, a.n_chunks); i++) s1 += cs[2 * i];
+            sh.P[j] = s1;
+        }
+        __syncthreads();
     }
-    for (int r = n4 * 4; r < n; r++) s = __fadd_rn(s, x[r]);
-    const float mean = __fdiv_rn(s, (float)n);
-    float var = 0.f;
-#pragma unroll 8
-    for (int i = 0; i < n4; i++) {
-        const float4 v = x4[i];
-        float d;
-        d = __fsub_rn(v.x, mean); var = __fadd_rn(var, __fmul_rn(d, d));
-        d = __fsub_rn(v.y, mean); var = __fadd_rn(var, __fmul_rn(d, d));
-        d = __fsub_rn(v.z, mean); var = __fadd_rn(var, __fmul_rn(d, d));
-        d = __fsub_rn(v.w, mean); var = __fadd_rn(var, __fmul_rn(d, d));
+    const float sum = exact_chain_sum(x, n, M, nch, sh, [](float v) { return v; }, pre);
+    const float mean = __fdiv_rn(sum, (float)n);
+    if (pre) {
+        const double m = mean;
+        for (int j = threadIdx.x; j < nch; j += ZN_THREADS) {
+            double s = 0.0;
+            for (int i = j * per; i < min((j + 1) * per, a.n_chunks); i++) {
+                const double cnt = (double)max(0, min(ZN_CHUNK_ROWS, n - i * ZN_CHUNK_ROWS));
+                s += cs[2 * i + 1] - 2.0 * m * cs[2 * i] + cnt * m * m;
+            }
+            sh.P[j] = s;
+        }
+        __syncthreads();
     }
-    for (int r = n4 * 4; r < n; r++) {
-        const float d = __fsub_rn(x[r], mean);
-        var = __fadd_rn(var, __fmul_rn(d, d));
+    const float var = exact_chain_sum(x, n, M, nch, sh, [mean](float v) {
+        const float d = __fsub_rn(v, mean);
+        return __fmul_rn(d, d);
+    }, pre);
+    if (threadIdx.x == 0) {
+        float sd = __fsqrt_rn(__fdiv_rn(var, (float)n));
+        if (sd < 1e-6f) sd = 1e-6f;
+        a.ms[t] = make_float2(mean, sd);
     }
-    float sd = __fsqrt_rn(__fdiv_rn(var, (float)n));
-    if (sd < 1e-6f) sd = 1e-6f;
-    a.ms[t] = make_float2(mean, sd);
 }
 
 /* z-score of row r, max over the group: triattention.c:240-247 */

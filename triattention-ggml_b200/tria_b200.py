@@ -112,6 +112,7 @@ def lib() -> C.CDLL:
         L.tria_select_noalloc.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int32,
                                           C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
                                           C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]
+        L.tria_znorm_stats.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]
         L.tria_score_kv_head_dev.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
                                              C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]
         _lib = L
@@ -168,6 +169,13 @@ def layer_budget(stats, layer, base_budget):
 # ---------------- device path ----------------
 
 NOALLOC_MAX_KEYS = 1 << 20
+
+
+def znorm_stats(x, stride, n, mean_std, stream=None):
+    """tria_znorm_stats: exact (mean, std) of each row of device array x."""
+    nn = np.ascontiguousarray(n, np.int32)
+    check(lib().tria_znorm_stats(_ptr(x), int(stride), nn.ctypes.data, int(nn.shape[0]),
+                                 _ptr(mean_std), _stream(stream)))
 
 
 def select_noalloc(scores, score_stride, n_rows, keep, kept_idx, kept_stride, n_kept,
