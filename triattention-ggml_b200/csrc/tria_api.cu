@@ -87,7 +87,11 @@ struct tria_ctx {
     uint32_t *keys = nullptr;
     int32_t *kept = nullptr;
     int32_t *cnt = nullptr;
+    double *csum = nullptr;              /* [units*G][n_chunks][2] */
+    int32_t n_chunks = 0;
+    bool csum_ready = false;             /* the last scoring pass filled csum */
     int64_t raw_stride = 0, cell_stride = 0;
+    int sm_count = 148;
     /* host-API staging */
     uint8_t *d_io = nullptr;
     size_t io_cap = 0;
@@ -155,6 +159,7 @@ extern "C" TRIA_API int tria_ctx_create(const tria_stats *s, int device, tria_ct
     tria_ctx *c = new (std::nothrow) tria_ctx;
     if (!c) FAIL(TRIA_ERR_NOMEM, "tria_ctx_create: host allocation failed");
     c->device = device;
+    cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
     c->L = s->num_layers; c->H = s->num_heads; c->KV = s->num_kv_heads;
     c->hd = s->head_dim; c->fc = s->freq_count; c->G = G;
     c->scales.assign(s->layer_budget_scales, s->layer_budget_scales + s->num_layers);
@@ -237,7 +242,9 @@ static int ensure_scratch(tria_ctx *c, int64_t units, int64_t cells, cudaStream_
     const size_t key_b = align256((size_t)units * stride * 4);
     const size_t kept_b = align256((size_t)units * stride * 4);
     const size_t cnt_b = align256((size_t)units * 4);
-    const size_t need = raw_b + ms_b + key_b + kept_b + cnt_b;
+    const int64_t n_chunks = std::max<int64_t>(1, (cells + ZN_CHUNK_ROWS - 1) / ZN_CHUNK_ROWS);
+    const size_t csum_b = align256((size_t)units * c->G * n_chunks * 2 * sizeof(double));
+    const size_t need = raw_b + ms_b + key_b + kept_b + cnt_b + csum_b;
     if (need > c->scratch_cap) {
         cudaDeviceSynchronize();      /* earlier calls may still use it, on any stream */
         if (c->d_scratch) cudaFree(c->d_scratch);
@@ -251,7 +258,9 @@ static int ensure_scratch(tria_ctx *c, int64_t units, int64_t cells, cudaStream_
     c->ms = (float2 *)p; p += ms_b;
     c->keys = (uint32_t *)p; p += key_b;
     c->kept = (int32_t *)p; p += kept_b;
-    c->cnt = (int32_t *)p;
+    c->cnt = (int32_t *)p; p += cnt_b;
+    c->csum = (double *)p;
+    c->n_chunks = (int32_t)n_chunks;
     c->raw_stride = stride;
     c->cell_stride = stride;
     if (c->pinned_cap < units + 1) {
@@ -391,8 +400,8 @@ static int launch_znorm(tria_ctx *c, int64_t unit0, int units, const int32_t *n_
     z.G = (int32_t)c->G;
     z.units = units;
     z.ms = c->ms + unit0 * c->G;
-    z.csum = nullptr;
-    z.n_chunks = 0;
+    z.csum = c->csum_ready ? c->csum + unit0 * c->G * c->n_chunks * 2 : nullptr;
+    z.n_chunks = c->n_chunks;
     for (int u = 0; u < units; u++) z.n_rows[u] = n_rows[unit0 + u];
     const int chains = units * (int)c->G;
     k_znorm_exact<<<chains, ZN_THREADS, 0, st>>>(z);
@@ -401,9 +410,112 @@ static int launch_znorm(tria_ctx *c, int64_t unit0, int units, const int32_t *n_
     return TRIA_OK;
 }
 
-/* Raw scores of every unit of `v`. */
+/* Shared-memory plan of k_score_ws for this view; stages == 0 when the view
+ * does not qualify (cell tiles must be contiguous 16-byte multiples, <= 8 kv
+ * heads, head_dim 128, positions 16-byte aligned with n_cells % 4 == 0). */
+static WsPlan ws_plan(const tria_ctx *c, const tria_kv_view *v) {
+    WsPlan p{};
+    const int64_t rb = view_row_bytes(v->type, (int)c->hd);
+    if (v->head_stride != rb || v->cell_stride != rb * v->n_head_kv) return p;
+    if (v->cell_stride % 16 || v->n_head_kv > WS_CWARPS || v->cell_stride * SC_T > (1 << 20)) return p;
+    if (v->n_cells % 4 || ((uintptr_t)v->pos & 15)) return p;
+    if (c->fc != 64) return p;
+    if (c->G != 1 && c->G != 2 && c->G != 4 && c->G != 5 && c->G != 6) return p;
+    p.cell_bytes = (int)v->cell_stride;
+    p.tab_rows = v->pos_shared ? SC_T : SC_T * v->n_head_kv;
+    p.pos_ints = p.tab_rows;
+    p.G = (int)c->G;
+    for (int s = 4; s >= 2; s--) {
+        p.stages = s;
+        if (p.total((int)c->fc) <= 220 * 1024) return p;
+    }
+    p.stages = 0;
+    return p;
+}
+
+template <int KT, int G>
+static int launch_ws_inst(const TmaScoreArgs &a, const WsPlan &plan, int grid, cudaStream_t st) {
+    auto fn = k_score_ws<KT, G>;
+    const int smem = plan.total(64);
+    CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    fn<<<grid, WS_THREADS, smem, st>>>(a, plan);
+    CUDA_TRY(cudaGetLastError());
+    return TRIA_OK;
+}
+
+template <int KT>
+static int launch_ws_g(int G, const TmaScoreArgs &a, const WsPlan &plan, int grid, cudaStream_t st) {
+    switch (G) {
+        case 1: return launch_ws_inst<KT, 1>(a, plan, grid, st);
+        case 2: return launch_ws_inst<KT, 2>(a, plan, grid, st);
+        case 4: return launch_ws_inst<KT, 4>(a, plan, grid, st);
+        case 5: return launch_ws_inst<KT, 5>(a, plan, grid, st);
+        case 6: return launch_ws_inst<KT, 6>(a, plan, grid, st);
+        default: FAIL(TRIA_ERR_UNSUPPORTED, "k_score_ws: gqa %d not instantiated", G);
+    }
+}
+
+static int launch_score_ws(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, int l0, int nl,
+                           int32_t cur_pos, const WsPlan &plan, cudaStream_t st) {
+    TmaScoreArgs *a = new (std::nothrow) TmaScoreArgs;
+    if (!a) FAIL(TRIA_ERR_NOMEM, "host allocation failed");
+    memset(a, 0, sizeof *a);
+    const int KV = v->n_head_kv;
+    int max_rows = 0;
+    for (int l = 0; l < nl; l++) {
+        a->k[l] = (const uint8_t *)v->k[l0 + l];
+        int lr = 0;
+        for (int h = 0; h < KV; h++) lr = std::max(lr, n_rows[(int64_t)(l0 + l) * KV + h]);
+        a->layer_rows[l] = lr;
+        max_rows = std::max(max_rows, lr);
+    }
+    for (int u = 0; u < nl * KV; u++) a->n_rows[u] = n_rows[(int64_t)l0 * KV + u];
+    a->cell_stride = v->cell_stride;
+    a->row_bytes = (int32_t)view_row_bytes(v->type, (int)c->hd);
+    a->pos = v->pos_shared ? v->pos : v->pos + (int64_t)l0 * KV * v->n_cells;
+    a->pos_shared = v->pos_shared ? 1 : 0;
+    a->n_cells = v->n_cells;
+    a->n_layer = nl;
+    a->n_head_kv = KV;
+    a->layer0 = v->layer0 + l0;
+    a->head0 = v->head0;
+    a->cur_pos = cur_pos;
+    a->H = (int32_t)c->H;
+    a->q = c->d_q;
+    a->table = reinterpret_cast<const float4 *>(c->d_table);
+    a->t_lo = c->t_lo;
+    a->t_len = c->t_len;
+    a->raw = c->raw + (int64_t)l0 * KV * c->G * c->raw_stride;
+    a->raw_stride = c->raw_stride;
+    a->csum = c->csum + (int64_t)l0 * KV * c->G * c->n_chunks * 2;
+    a->n_chunks = c->n_chunks;
+    a->status = c->d_status;
+    a->tiles_per_layer = (max_rows + SC_T - 1) / SC_T;
+    a->n_items = a->tiles_per_layer * nl;
+    int rc = TRIA_OK;
+    if (a->n_items > 0) {
+        const int grid = std::min(a->n_items, c->sm_count);
+        rc = v->type == TRIA_TYPE_F16 ? launch_ws_g<KT_F16>((int)c->G, *a, plan, grid, st)
+                                      : launch_ws_g<KT_Q8_0>((int)c->G, *a, plan, grid, st);
+        if (!rc) c->launches++;
+    }
+    delete a;
+    return rc;
+}
+
+/* Raw scores of every unit of `v` (and, on the warp-specialised path, the
+ * z-norm predictor sums). */
 static int run_score(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, int32_t cur_pos, int kt,
                      cudaStream_t st) {
+    const WsPlan plan = kt == KT_F32SPLIT ? WsPlan{} : ws_plan(c, v);
+    c->csum_ready = plan.stages > 0;
+    if (plan.stages > 0) {
+        const int64_t units = (int64_t)v->n_layer * v->n_head_kv;
+        CUDA_TRY(cudaMemsetAsync(c->csum, 0, (size_t)units * c->G * c->n_chunks * 2 * sizeof(double), st));
+        return for_layer_chunks(v, [&](int l0, int nl) -> int {
+            return launch_score_ws(c, v, n_rows, l0, nl, cur_pos, plan, st);
+        });
+    }
     return for_layer_chunks(v, [&](int l0, int nl) -> int {
         ScoreArgs *a = new (std::nothrow) ScoreArgs;
         if (!a) FAIL(TRIA_ERR_NOMEM, "host allocation failed");
@@ -755,6 +867,7 @@ static int score_split(tria_ctx *c, const float *k_re, const float *k_im, const 
     delete a;
     if (rc) return rc;
     int32_t nr[1] = {n};
+    c->csum_ready = false;
     if ((rc = launch_znorm(c, 0, 1, nr, st))) return rc;
     ZmaxArgs z;
     z.raw = c->raw;

@@ -12,7 +12,7 @@
  *                  table depends only on the integer delta d = cur_pos - pos.
  *                  It is built once per context and reused by every layer,
  *                  head and step (like a RoPE cache).
- *   k_score_raw    streams the K cache once.  Per row it forms
+ *   k_score_ws     (and k_score_raw for other layouts) streams the K cache once.  Per row it forms
  *                     X_f = C kr + S ki,  Y_f = C ki - S kr,  |k_f|
  *                  and for each query head g of the group
  *                     raw_g = (sum_f qr_gf X_f + qi_gf Y_f) / 17 + sum_f res_gf |k_f|
@@ -48,6 +48,7 @@ constexpr int N_OFF = 17;
 constexpr int SCORE_THREADS = 256;
 constexpr int SCORE_CHUNK = 256;       /* cells per CTA (per layer) */
 constexpr int SELECT_THREADS = 1024;
+constexpr int ZN_CHUNK_ROWS = 128;     /* rows per z-norm predictor sum written by the scoring kernel */
 
 /* ------------------------------------------------------------------ */
 /* Delta table                                                          */
@@ -71,7 +72,10 @@ __global__ void k_build_table(float2 *__restrict__ T, int64_t d_lo, int64_t n_d,
         c += cd;
         s += sd;
     }
-    T[i] = make_float2((float)c, (float)s);
+    /* layout per frequency pair p = f/2: float4 (C_2p, C_2p+1, S_2p, S_2p+1) */
+    float *Tf = reinterpret_cast<float *>(T) + di * 2 * fc + 4 * (f >> 1) + (f & 1);
+    Tf[0] = (float)c;
+    Tf[2] = (float)s;
 }
 
 /* ------------------------------------------------------------------ */
@@ -85,7 +89,7 @@ struct ScoreArgs {
     const int32_t *pos;
     int32_t pos_shared, n_cells, n_layer, n_head_kv, layer0, head0, cur_pos, H, fc;
     const float *q;                       /* [L][H][3][fc]: qr, qi, max(0, qam - qma) */
-    const float2 *table;                  /* [t_len][fc] */
+    const float2 *table;                  /* [t_len][fc]: per pair float4 (C0, C1, S0, S1) */
     int64_t t_lo, t_len;
     float *raw;                           /* [units*G][raw_stride] */
     int64_t raw_stride;
@@ -199,11 +203,11 @@ __global__ void __launch_bounds__(SCORE_THREADS) k_score_raw(const ScoreArgs a) 
                     for (int g = 0; g < G; g++) { acc[g] = 0.f; ext[g] = 0.f; }
 #pragma unroll
                     for (int t2 = 0; t2 < FPL / 2; t2++) {
-                        const float4 cs = T4[t2];      /* (C, S) of pairs 2*t2, 2*t2+1 */
+                        const float4 cs = T4[t2];      /* (C0, C1, S0, S1) of pairs 2*t2, 2*t2+1 */
 #pragma unroll
                         for (int e = 0; e < 2; e++) {
                             const int t = 2 * t2 + e;
-                            const float C = e ? cs.z : cs.x, S = e ? cs.w : cs.y;
+                            const float C = e ? cs.y : cs.x, S = e ? cs.w : cs.z;
                             const float X = fmaf(C, kr[t], S * ki[t]);
                             const float Y = fmaf(C, ki[t], -(S * kr[t]));
                             const float ka = sqrt_approx(fmaf(kr[t], kr[t], ki[t] * ki[t]));
@@ -229,6 +233,429 @@ __global__ void __launch_bounds__(SCORE_THREADS) k_score_raw(const ScoreArgs a) 
             }
         }
     }
+}
+
+/* ------------------------------------------------------------------ */
+/* Scoring, TMA-fed and warp-specialised (views whose cell tiles are   */
+/* contiguous: llama.cpp's layout), head_dim 128                        */
+/* ------------------------------------------------------------------ */
+
+constexpr int ST_TIMEOUT = 2;          /* status bit: a pipeline wait gave up */
+constexpr int SC_T = 16;               /* cells per work item (tile) */
+constexpr int WS_CWARPS = 8;           /* consumer warps: one kv head each */
+constexpr int WS_THREADS = (WS_CWARPS + 1) * 32;   /* + one producer warp */
+constexpr int WS_POS_RING = 8;         /* positions are fetched this many items ahead */
+
+struct TmaScoreArgs {
+    const uint8_t *k[TRIA_MAX_LAYERS];
+    int64_t cell_stride;                  /* == n_head_kv * row_bytes */
+    int32_t row_bytes;
+    const int32_t *pos;
+    int32_t pos_shared, n_cells, n_layer, n_head_kv, layer0, head0, cur_pos, H;
+    const float *q;                       /* [L][H][3][fc] */
+    const float4 *table;                  /* [t_len][fc/2] (C0, C1, S0, S1) */
+    int64_t t_lo, t_len;
+    float *raw;
+    int64_t raw_stride;
+    double *csum;                         /* [units*G][n_chunks][2]: sum, sum of squares per 128 rows */
+    int32_t n_chunks;
+    int32_t *status;
+    int32_t tiles_per_layer, n_items;
+    int32_t layer_rows[TRIA_MAX_LAYERS];  /* max rows over the layer's heads */
+    int32_t n_rows[TRIA_MAX_UNITS];
+};
+
+/* Shared-memory plan of k_score_ws, shared by host and device. */
+struct WsPlan {
+    int stages, cell_bytes, tab_rows, pos_ints, G;
+    __host__ __device__ int k_bytes() const { return SC_T * cell_bytes; }
+    __host__ __device__ int tab_bytes(int fc) const { return tab_rows * fc * 8; }
+    __host__ __device__ int stage_bytes(int fc) const { return k_bytes() + tab_bytes(fc) + pos_ints * 4; }
+    __host__ __device__ int out_bytes() const { return WS_CWARPS * G * SC_T * 4; }
+    __host__ __device__ int ring_bytes() const { return WS_POS_RING * pos_ints * 4; }
+    __host__ __device__ int total(int fc) const {
+        return stages * stage_bytes(fc) + ring_bytes() + out_bytes() + WS_CWARPS * G * 16 +
+               (2 * stages + WS_POS_RING) * 8;
+    }
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t *bar, uint32_t bytes) {
+    uint64_t st;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 %0, [%1], %2;"
+                 : "=l"(st) : "r"(smem_u32(bar)), "r"(bytes) : "memory");
+    asm volatile("" ::"l"(st));
+}
+__device__ __forceinline__ void mbar_expect(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    uint64_t st;
+    asm volatile("mbarrier.arrive.shared::cta.b64 %0, [%1];" : "=l"(st) : "r"(smem_u32(bar)) : "memory");
+    asm volatile("" ::"l"(st));
+}
+/* Non-multicast bulk copy global -> this CTA's shared memory. */
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+/* Wait for a phase of `bar`, giving up after ~2^31 cycles (about a second). */
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_try(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try(bar, parity))
+        if (clock64() - t0 > (1ll << 31)) return false;
+    return true;
+}
+
+typedef unsigned long long f2_t;          /* two packed fp32 for the f32x2 instructions */
+__device__ __forceinline__ f2_t pk(float a, float b) {
+    f2_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk(f2_t r, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ f2_t fma2(f2_t a, f2_t b, f2_t c) {
+    f2_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ f2_t mul2(f2_t a, f2_t b) {
+    f2_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ f2_t neg2(f2_t x) { return x ^ 0x8000000080000000ull; }
+/* Two packed halves -> two packed floats. */
+__device__ __forceinline__ f2_t h2_to_f2(uint32_t h) {
+    f2_t r;
+    asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 a, b;\n\tmov.b32 {lo, hi}, %1;\n\t"
+        "cvt.f32.f16 a, lo;\n\tcvt.f32.f16 b, hi;\n\tmov.b64 %0, {a, b};\n\t}" : "=l"(r) : "r"(h));
+    return r;
+}
+
+/* Frequency pair q (dims 2q, 2q+1) of the real and imaginary halves of a staged row. */
+template <int KT, int FC>
+__device__ __forceinline__ void row_pair(const uint8_t *row, int q, f2_t &kr, f2_t &ki) {
+    if constexpr (KT == KT_F16) {
+        kr = h2_to_f2(*reinterpret_cast<const uint32_t *>(row + 4 * q));
+        ki = h2_to_f2(*reinterpret_cast<const uint32_t *>(row + 2 * FC + 4 * q));
+    } else {                                             /* q8_0 block {f16 d; int8 q[32]} */
+        const int dr = 2 * q, dm = FC + 2 * q;
+        const uint8_t *br = row + (dr >> 5) * 34, *bm = row + (dm >> 5) * 34;
+        const float sr = __half2float(*reinterpret_cast<const __half *>(br));
+        const float sm = __half2float(*reinterpret_cast<const __half *>(bm));
+        const char2 vr = *reinterpret_cast<const char2 *>(br + 2 + (dr & 31));
+        const char2 vm = *reinterpret_cast<const char2 *>(bm + 2 + (dm & 31));
+        kr = pk((float)vr.x * sr, (float)vr.y * sr);
+        ki = pk((float)vm.x * sm, (float)vm.y * sm);
+    }
+}
+
+/*
+ * Warp-specialised scoring (head_dim 128: fc = 64 frequencies, 32 pairs).
+ *
+ * Warp WS_CWARPS is the producer.  Positions of work item k arrive in a
+ * small ring by bulk copy WS_POS_RING-1 items ahead.  For item k (a 16-cell
+ * tile of one layer; a CTA's items are contiguous) it waits until the
+ * consumers released the stage, then bulk-copies (cp.async.bulk, no
+ * multicast) the whole K tile in one copy and the delta-table rows
+ * T[cur_pos - pos]: one copy of a contiguous range when the tile's positions
+ * are consecutive (a fresh cache, appended rows), else one copy per row; it
+ * records each row's table slot in the stage.  The stage's `full` barrier
+ * completes when all bytes landed.  Few large copies matter: the copy engine
+ * streams 32 KB tiles at HBM speed but not sixteen 2 KB pieces.
+ *
+ * Each consumer warp scores one kv head, four cells per pass: 8 lanes per
+ * cell, lane j of cell slot s owning the frequency pairs j + 8*((i + s) & 3),
+ * i = 0..3, so each load instruction reads four different 32-byte windows of
+ * K (no bank conflicts) and 128 contiguous bytes of each cell's table row.
+ * The lane's q-centre terms (pre-scaled by 1/17) and norm terms for its pairs
+ * stay in registers for the whole layer; the math runs as packed f32x2 FMAs;
+ * the G sums are reduced across the 8 lanes with a transposing butterfly,
+ * staged, written per tile and folded into per-128-row sums for the z-norm
+ * kernel's binade prediction.  Every wait is bounded (ST_TIMEOUT).
+ */
+template <int KT, int G>
+__global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a, const WsPlan plan) {
+    constexpr int FC = 64, NQ = FC / 2, QPL = 4;        /* pairs per lane */
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int KV = a.n_head_kv;
+    const int S = plan.stages;
+    const int stage_bytes = plan.stage_bytes(FC);
+    uint8_t *stages = smem;
+    int32_t *ring = reinterpret_cast<int32_t *>(smem + S * stage_bytes);              /* [WS_POS_RING][pos_ints] */
+    float *outbuf = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ring) + plan.ring_bytes());
+    double *csums = reinterpret_cast<double *>(reinterpret_cast<uint8_t *>(outbuf) + plan.out_bytes());
+    uint64_t *full = reinterpret_cast<uint64_t *>(csums + WS_CWARPS * G * 2);
+    uint64_t *empty = full + S;
+    uint64_t *posbar = empty + S;
+    __shared__ volatile int s_abort;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        for (int i = 0; i < S; i++) { mbar_init(&full[i], 1); mbar_init(&empty[i], WS_CWARPS); }
+        for (int i = 0; i < WS_POS_RING; i++) mbar_init(&posbar[i], 1);
+        s_abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    const int per_cta = (a.n_items + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int it0 = (int)blockIdx.x * per_cta;
+    const int n_mine = max(0, min(per_cta, a.n_items - it0));
+    auto item_of = [&](int k, int &l, int &c0) -> int {
+        const int it = it0 + k;
+        l = it / a.tiles_per_layer;
+        c0 = (it - l * a.tiles_per_layer) * SC_T;
+        return max(0, min(SC_T, a.layer_rows[l] - c0));
+    };
+
+    if (warp == WS_CWARPS) {
+        /* ---------------- producer ---------------- */
+        /* positions of item kk -> ring slot kk % WS_POS_RING, one bulk copy per head row */
+        auto fetch_pos = [&](int kk) {
+            int l, c0;
+            const int cells = item_of(kk, l, c0);
+            uint64_t *bar = &posbar[kk % WS_POS_RING];
+            const int nrow = cells == 0 ? 0 : (a.pos_shared ? 1 : KV);
+            const uint32_t pb = (uint32_t)((cells + 3) / 4 * 16);   /* whole 16-byte groups (n_cells % 4 == 0) */
+            if (lane == 0) mbar_arrive_tx(bar, pb * nrow);
+            __syncwarp();
+            if (lane < nrow) {
+                const int32_t *src = a.pos_shared ? a.pos + c0 : a.pos + (int64_t)(l * KV + lane) * a.n_cells + c0;
+                bulk_g2s(ring + (kk % WS_POS_RING) * plan.pos_ints + lane * SC_T, src, pb, bar);
+            }
+        };
+        int pos_issued = 0;                              /* items whose positions were requested */
+        for (; pos_issued < min(WS_POS_RING - 1, n_mine); pos_issued++) fetch_pos(pos_issued);
+        int k = 0;
+        for (; k < n_mine && !s_abort; k++) {
+            const int st = k % S;
+            if (pos_issued < n_mine) fetch_pos(pos_issued++);   /* ring slot of item k-1: done with */
+            if (!mbar_wait(&posbar[k % WS_POS_RING], (uint32_t)((k / WS_POS_RING) & 1)) ||
+                !mbar_wait(&empty[st], (uint32_t)(((k / S) & 1) ^ 1))) {
+                if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
+                s_abort = 1;
+                break;
+            }
+            /* the consumers' reads of this stage happen before these async writes */
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            int l, c0;
+            const int cells = item_of(k, l, c0);
+            uint8_t *sb = stages + st * stage_bytes;
+            float4 *tab = reinterpret_cast<float4 *>(sb + plan.k_bytes());
+            int32_t *slot = reinterpret_cast<int32_t *>(sb + plan.k_bytes() + plan.tab_bytes(FC));
+            /* Table rows per head row (or the shared row): one contiguous copy when
+             * the positions are consecutive (d falls by one per cell), else one
+             * copy per cell.  slot[] gets each (head, cell) row's table slot, or
+             * -1 when its delta is outside the table. */
+            const int nrows = cells == 0 ? 0 : (a.pos_shared ? 1 : KV);
+            const int32_t *rp = ring + (k % WS_POS_RING) * plan.pos_ints;
+            for (int hh = 0; hh < nrows; hh++) {
+                const int32_t *hp = rp + hh * SC_T;
+                const int p0 = hp[0];
+                bool consec = true;
+                for (int c = lane; c < cells; c += 32) consec &= hp[c] == p0 + c;
+                consec = __all_sync(0xffffffffu, consec);
+                const int64_t dhi = (int64_t)a.cur_pos - p0 - a.t_lo;             /* row of cell 0 */
+                const int64_t dlo = dhi - (cells - 1);                             /* row of the last cell */
+                if (consec && dlo >= 0 && dhi < a.t_len) {
+                    if (lane < cells) slot[hh * SC_T + lane] = hh * SC_T + (cells - 1 - lane);
+                    if (lane == 0) {
+                        mbar_expect(&full[st], (uint32_t)cells * FC * 8);
+                        bulk_g2s(tab + hh * SC_T * NQ, a.table + dlo * NQ, (uint32_t)cells * FC * 8, &full[st]);
+                    }
+                } else {
+                    bool ok = false;
+                    int64_t di = 0;
+                    if (lane < cells) {
+                        di = (int64_t)a.cur_pos - hp[lane] - a.t_lo;
+                        ok = di >= 0 && di < a.t_len;
+                        slot[hh * SC_T + lane] = ok ? hh * SC_T + lane : -1;
+                    }
+                    const unsigned okm = __ballot_sync(0xffffffffu, ok);
+                    if (lane == 0) {
+                        mbar_expect(&full[st], (uint32_t)__popc(okm) * FC * 8);
+                        if (__popc(okm) != cells) atomicOr(a.status, ST_POSITION);
+                    }
+                    __syncwarp();
+                    if (ok) bulk_g2s(tab + (hh * SC_T + lane) * NQ, a.table + di * NQ, FC * 8, &full[st]);
+                }
+                __syncwarp();
+            }
+            if (lane == 0 && cells > 0) {
+                mbar_expect(&full[st], (uint32_t)(cells * a.cell_stride));
+                bulk_g2s(sb, a.k[l] + (int64_t)c0 * a.cell_stride, (uint32_t)(cells * a.cell_stride), &full[st]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[st]);       /* also publishes the slot stores */
+        }
+        /* drain: every copy issued must land before the CTA exits */
+        if (lane == 0) {
+            for (int kk = max(0, k - S); kk < k; kk++)
+                mbar_wait(&full[kk % S], (uint32_t)((kk / S) & 1));
+            for (int kk = k; kk < pos_issued; kk++)
+                mbar_wait(&posbar[kk % WS_POS_RING], (uint32_t)((kk / WS_POS_RING) & 1));
+        }
+        return;
+    }
+
+    /* ---------------- consumers ---------------- */
+    const int j = lane & 7, cs4 = lane >> 3;             /* pair owner, cell of the pass */
+    const int wph = max(1, WS_CWARPS / KV);              /* warps per head */
+    const bool active = warp < KV * wph;
+    const int h = active ? warp % KV : 0, sub = warp / KV;
+    const int cpw = (SC_T + wph - 1) / wph;              /* cells of a tile per warp */
+    const float inv17 = 1.0f / 17.0f;
+    float *ob = outbuf + warp * G * SC_T;                /* [g][cell] */
+    double *csw = csums + warp * G * 2;
+    if (lane < G) { csw[2 * lane] = 0.0; csw[2 * lane + 1] = 0.0; }
+    f2_t qr[G][QPL], qi[G][QPL], qx[G][QPL];
+    int cur_l = -1, cur_chunk = -1, chunk_u = 0;
+    auto flush = [&]() {
+        if (cur_chunk >= 0 && active && lane < G) {
+            double *cs = a.csum + (((int64_t)chunk_u * G + lane) * a.n_chunks + cur_chunk) * 2;
+            atomicAdd(cs, csw[2 * lane]);
+            atomicAdd(cs + 1, csw[2 * lane + 1]);
+            csw[2 * lane] = 0.0;
+            csw[2 * lane + 1] = 0.0;
+        }
+    };
+
+    for (int k = 0; k < n_mine; k++) {
+        const int st = k % S;
+        int l, c0;
+        const int cells = item_of(k, l, c0);
+        if (!mbar_wait(&full[st], (uint32_t)((k / S) & 1))) {
+            if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
+            s_abort = 1;
+        }
+        if (s_abort) break;
+        const uint8_t *sb = stages + st * stage_bytes;
+        const float4 *tab = reinterpret_cast<const float4 *>(sb + plan.k_bytes());
+        const int32_t *slot = reinterpret_cast<const int32_t *>(sb + plan.k_bytes() + plan.tab_bytes(FC));
+        const int cbeg = sub * cpw;
+        const int u = l * KV + h;
+        const int cend = active ? min(min(cells, a.n_rows[u] - c0), cbeg + cpw) : 0;
+        if (cbeg < cend) {
+            if (l != cur_l) {                                  /* this lane's q terms for layer l */
+                cur_l = l;
+                const int ml = a.layer0 + l, mh = a.head0 + h;
+                const float *src = a.q + ((size_t)(ml * a.H + mh * G) * 3) * FC;
+#pragma unroll
+                for (int g = 0; g < G; g++)
+#pragma unroll
+                    for (int i = 0; i < QPL; i++) {
+                        const int q = j + 8 * ((i + cs4) & 3);     /* rotated: the pass's 4 cells hit 4 windows */
+                        const float2 r = *reinterpret_cast<const float2 *>(src + g * 3 * FC + 2 * q);
+                        const float2 m = *reinterpret_cast<const float2 *>(src + g * 3 * FC + FC + 2 * q);
+                        qr[g][i] = pk(r.x * inv17, r.y * inv17);
+                        qi[g][i] = pk(m.x * inv17, m.y * inv17);
+                        qx[g][i] = *reinterpret_cast<const f2_t *>(src + g * 3 * FC + 2 * FC + 2 * q);
+                    }
+            }
+            const int chunk = c0 / ZN_CHUNK_ROWS;
+            if (chunk != cur_chunk || u != chunk_u) {
+                flush();
+                cur_chunk = chunk;
+                chunk_u = u;
+            }
+            const int hoff = h * a.row_bytes;
+            for (int cb = cbeg; cb < cend; cb += 4) {
+                const int c = cb + cs4;
+                const bool valid = c < cend;
+                float v[G];
+#pragma unroll
+                for (int g = 0; g < G; g++) v[g] = 0.f;
+                const int ts = valid ? slot[a.pos_shared ? c : h * SC_T + c] : -1;
+                if (ts >= 0) {
+                    const float4 *T = tab + ts * NQ;
+                    const uint8_t *row = sb + c * a.cell_stride + hoff;
+                    f2_t acc[G];
+#pragma unroll
+                    for (int g = 0; g < G; g++) acc[g] = 0ull;
+#pragma unroll
+                    for (int i = 0; i < QPL; i++) {
+                        const int q = j + 8 * ((i + cs4) & 3);
+                        const ulonglong2 cs = *reinterpret_cast<const ulonglong2 *>(T + q);   /* (C, S) pairs */
+                        f2_t kr, ki;
+                        row_pair<KT, FC>(row, q, kr, ki);
+                        const f2_t X = fma2(cs.x, kr, mul2(cs.y, ki));
+                        const f2_t Y = fma2(cs.x, ki, mul2(cs.y, neg2(kr)));
+                        const f2_t m2 = fma2(kr, kr, mul2(ki, ki));
+                        float m0, m1;
+                        upk(m2, m0, m1);
+                        const f2_t ka = pk(sqrt_approx(m0), sqrt_approx(m1));
+#pragma unroll
+                        for (int g = 0; g < G; g++) {
+                            acc[g] = fma2(qr[g][i], X, acc[g]);
+                            acc[g] = fma2(qi[g][i], Y, acc[g]);
+                            acc[g] = fma2(qx[g][i], ka, acc[g]);
+                        }
+                    }
+#pragma unroll
+                    for (int g = 0; g < G; g++) {
+                        float a0, a1;
+                        upk(acc[g], a0, a1);
+                        v[g] = a0 + a1;
+                    }
+                }
+                /* reduce over the cell's 8 lanes: groups of 4 query heads transposed */
+#pragma unroll
+                for (int g0 = 0; g0 + 4 <= G; g0 += 4) {
+                    const bool b1 = (j >> 2) & 1, b0 = (j >> 1) & 1;
+                    float x0 = b1 ? v[g0 + 2] : v[g0], x1 = b1 ? v[g0 + 3] : v[g0 + 1];
+                    const float y0 = b1 ? v[g0] : v[g0 + 2], y1 = b1 ? v[g0 + 1] : v[g0 + 3];
+                    x0 += __shfl_xor_sync(0xffffffffu, y0, 4);
+                    x1 += __shfl_xor_sync(0xffffffffu, y1, 4);
+                    float kk = b0 ? x1 : x0;
+                    const float oo = b0 ? x0 : x1;
+                    kk += __shfl_xor_sync(0xffffffffu, oo, 2);
+                    kk += __shfl_xor_sync(0xffffffffu, kk, 1);
+                    if (valid && (j & 1) == 0) ob[(g0 + 2 * b1 + b0) * SC_T + c] = kk;
+                }
+#pragma unroll
+                for (int g = G - G % 4; g < G; g++) {
+                    float kk = v[g];
+                    kk += __shfl_xor_sync(0xffffffffu, kk, 4);
+                    kk += __shfl_xor_sync(0xffffffffu, kk, 2);
+                    kk += __shfl_xor_sync(0xffffffffu, kk, 1);
+                    if (valid && j == 0) ob[g * SC_T + c] = kk;
+                }
+            }
+            __syncwarp();
+            /* cells [cbeg, cend): write out, fold into the chunk sums */
+            for (int i = lane; i < G * cpw; i += 32) {
+                const int g = i / cpw, c = cbeg + (i - g * cpw);
+                if (c < cend) a.raw[((int64_t)u * G + g) * a.raw_stride + c0 + c] = ob[g * SC_T + c];
+            }
+            if (lane < G) {
+                double s1 = csw[2 * lane], s2 = csw[2 * lane + 1];
+                for (int c = cbeg; c < cend; c++) {
+                    const double x = ob[lane * SC_T + c];
+                    s1 += x;
+                    s2 += x * x;
+                }
+                csw[2 * lane] = s1;
+                csw[2 * lane + 1] = s2;
+            }
+            __syncwarp();
+        }
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    flush();
 }
 
 /* ------------------------------------------------------------------ */
@@ -258,7 +685,6 @@ __global__ void __launch_bounds__(SCORE_THREADS) k_score_raw(const ScoreArgs a) 
 
 constexpr int ZN_THREADS = 128;
 constexpr int ZN_MAXCH = 512;          /* chunks per chain kept in shared memory */
-constexpr int ZN_CHUNK_ROWS = 128;     /* rows per predictor sum written by the scoring kernel */
 
 struct ZArgs {
     const float *raw;
