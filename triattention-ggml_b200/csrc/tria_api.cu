@@ -87,9 +87,6 @@ struct tria_ctx {
     uint32_t *keys = nullptr;
     int32_t *kept = nullptr;
     int32_t *cnt = nullptr;
-    double *csum = nullptr;              /* [units*G][n_chunks][2] */
-    int32_t n_chunks = 0;
-    bool csum_ready = false;             /* the last scoring pass filled csum */
     int64_t raw_stride = 0, cell_stride = 0;
     int sm_count = 148;
     /* host-API staging */
@@ -242,9 +239,7 @@ static int ensure_scratch(tria_ctx *c, int64_t units, int64_t cells, cudaStream_
     const size_t key_b = align256((size_t)units * stride * 4);
     const size_t kept_b = align256((size_t)units * stride * 4);
     const size_t cnt_b = align256((size_t)units * 4);
-    const int64_t n_chunks = std::max<int64_t>(1, (cells + ZN_CHUNK_ROWS - 1) / ZN_CHUNK_ROWS);
-    const size_t csum_b = align256((size_t)units * c->G * n_chunks * 2 * sizeof(double));
-    const size_t need = raw_b + ms_b + key_b + kept_b + cnt_b + csum_b;
+    const size_t need = raw_b + ms_b + key_b + kept_b + cnt_b;
     if (need > c->scratch_cap) {
         cudaDeviceSynchronize();      /* earlier calls may still use it, on any stream */
         if (c->d_scratch) cudaFree(c->d_scratch);
@@ -258,9 +253,7 @@ static int ensure_scratch(tria_ctx *c, int64_t units, int64_t cells, cudaStream_
     c->ms = (float2 *)p; p += ms_b;
     c->keys = (uint32_t *)p; p += key_b;
     c->kept = (int32_t *)p; p += kept_b;
-    c->cnt = (int32_t *)p; p += cnt_b;
-    c->csum = (double *)p;
-    c->n_chunks = (int32_t)n_chunks;
+    c->cnt = (int32_t *)p;
     c->raw_stride = stride;
     c->cell_stride = stride;
     if (c->pinned_cap < units + 1) {
@@ -400,11 +393,10 @@ static int launch_znorm(tria_ctx *c, int64_t unit0, int units, const int32_t *n_
     z.G = (int32_t)c->G;
     z.units = units;
     z.ms = c->ms + unit0 * c->G;
-    z.csum = c->csum_ready ? c->csum + unit0 * c->G * c->n_chunks * 2 : nullptr;
-    z.n_chunks = c->n_chunks;
+    z.status = c->d_status;
     for (int u = 0; u < units; u++) z.n_rows[u] = n_rows[unit0 + u];
     const int chains = units * (int)c->G;
-    k_znorm_exact<<<chains, ZN_THREADS, 0, st>>>(z);
+    k_znorm_walk<<<(chains + ZW_WARPS - 1) / ZW_WARPS, ZW_WARPS * 32, 0, st>>>(z);
     CUDA_TRY(cudaGetLastError());
     c->launches++;
     return TRIA_OK;
@@ -487,8 +479,6 @@ static int launch_score_ws(tria_ctx *c, const tria_kv_view *v, const int32_t *n_
     a->t_len = c->t_len;
     a->raw = c->raw + (int64_t)l0 * KV * c->G * c->raw_stride;
     a->raw_stride = c->raw_stride;
-    a->csum = c->csum + (int64_t)l0 * KV * c->G * c->n_chunks * 2;
-    a->n_chunks = c->n_chunks;
     a->status = c->d_status;
     a->tiles_per_layer = (max_rows + SC_T - 1) / SC_T;
     a->n_items = a->tiles_per_layer * nl;
@@ -503,15 +493,11 @@ static int launch_score_ws(tria_ctx *c, const tria_kv_view *v, const int32_t *n_
     return rc;
 }
 
-/* Raw scores of every unit of `v` (and, on the warp-specialised path, the
- * z-norm predictor sums). */
+/* Raw scores of every unit of `v`. */
 static int run_score(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, int32_t cur_pos, int kt,
                      cudaStream_t st) {
     const WsPlan plan = kt == KT_F32SPLIT ? WsPlan{} : ws_plan(c, v);
-    c->csum_ready = plan.stages > 0;
     if (plan.stages > 0) {
-        const int64_t units = (int64_t)v->n_layer * v->n_head_kv;
-        CUDA_TRY(cudaMemsetAsync(c->csum, 0, (size_t)units * c->G * c->n_chunks * 2 * sizeof(double), st));
         return for_layer_chunks(v, [&](int l0, int nl) -> int {
             return launch_score_ws(c, v, n_rows, l0, nl, cur_pos, plan, st);
         });
@@ -799,10 +785,9 @@ extern "C" TRIA_API int tria_znorm_stats(const float *x, int64_t stride, const i
         z.G = 1;
         z.units = cn;
         z.ms = reinterpret_cast<float2 *>(mean_std) + c0;
-        z.csum = nullptr;
-        z.n_chunks = 0;
+        z.status = nullptr;
         for (int i = 0; i < cn; i++) z.n_rows[i] = n[c0 + i];
-        k_znorm_exact<<<cn, ZN_THREADS, 0, (cudaStream_t)stream>>>(z);
+        k_znorm_walk<<<(cn + ZW_WARPS - 1) / ZW_WARPS, ZW_WARPS * 32, 0, (cudaStream_t)stream>>>(z);
         CUDA_TRY(cudaGetLastError());
     }
     return TRIA_OK;
@@ -867,7 +852,6 @@ static int score_split(tria_ctx *c, const float *k_re, const float *k_im, const 
     delete a;
     if (rc) return rc;
     int32_t nr[1] = {n};
-    c->csum_ready = false;
     if ((rc = launch_znorm(c, 0, 1, nr, st))) return rc;
     ZmaxArgs z;
     z.raw = c->raw;

@@ -18,9 +18,10 @@
  *                     raw_g = (sum_f qr_gf X_f + qi_gf Y_f) / 17 + sum_f res_gf |k_f|
  *                  which is triattention.c:156-192 with the offset sum moved
  *                  into the table (rel_r cos - rel_i sin summed over o).
- *   k_znorm_exact  mean and variance bit-identical to the reference's
- *                  sequential fp32 chains (triattention.c:228-236), computed
- *                  as chunked ulp-grid translations; IEEE div/sqrt, clamp 1e-6.
+ *   k_znorm_walk   mean and variance bit-identical to the reference's
+ *                  sequential fp32 chains (triattention.c:228-236), a warp
+ *                  advancing a chain 512 elements per step as ulp-grid
+ *                  translations; IEEE div/sqrt, std clamp 1e-6.
  *   k_select       z-score max over the group (triattention.c:240-247), an
  *                  order-preserving 32-bit key, 8-bit radix select of the
  *                  keep-th largest key, ties to the lowest rows, and an
@@ -48,7 +49,6 @@ constexpr int N_OFF = 17;
 constexpr int SCORE_THREADS = 256;
 constexpr int SCORE_CHUNK = 256;       /* cells per CTA (per layer) */
 constexpr int SELECT_THREADS = 1024;
-constexpr int ZN_CHUNK_ROWS = 128;     /* rows per z-norm predictor sum written by the scoring kernel */
 
 /* ------------------------------------------------------------------ */
 /* Delta table                                                          */
@@ -257,8 +257,6 @@ struct TmaScoreArgs {
     int64_t t_lo, t_len;
     float *raw;
     int64_t raw_stride;
-    double *csum;                         /* [units*G][n_chunks][2]: sum, sum of squares per 128 rows */
-    int32_t n_chunks;
     int32_t *status;
     int32_t tiles_per_layer, n_items;
     int32_t layer_rows[TRIA_MAX_LAYERS];  /* max rows over the layer's heads */
@@ -274,8 +272,7 @@ struct WsPlan {
     __host__ __device__ int out_bytes() const { return WS_CWARPS * G * SC_T * 4; }
     __host__ __device__ int ring_bytes() const { return WS_POS_RING * pos_ints * 4; }
     __host__ __device__ int total(int fc) const {
-        return stages * stage_bytes(fc) + ring_bytes() + out_bytes() + WS_CWARPS * G * 16 +
-               (2 * stages + WS_POS_RING) * 8;
+        return stages * stage_bytes(fc) + ring_bytes() + out_bytes() + (2 * stages + WS_POS_RING) * 8;
     }
 };
 
@@ -384,8 +381,7 @@ __device__ __forceinline__ void row_pair(const uint8_t *row, int q, f2_t &kr, f2
  * The lane's q-centre terms (pre-scaled by 1/17) and norm terms for its pairs
  * stay in registers for the whole layer; the math runs as packed f32x2 FMAs;
  * the G sums are reduced across the 8 lanes with a transposing butterfly,
- * staged, written per tile and folded into per-128-row sums for the z-norm
- * kernel's binade prediction.  Every wait is bounded (ST_TIMEOUT).
+ * staged and written per tile.  Every wait is bounded (ST_TIMEOUT).
  */
 template <int KT, int G>
 __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a, const WsPlan plan) {
@@ -397,8 +393,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
     uint8_t *stages = smem;
     int32_t *ring = reinterpret_cast<int32_t *>(smem + S * stage_bytes);              /* [WS_POS_RING][pos_ints] */
     float *outbuf = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ring) + plan.ring_bytes());
-    double *csums = reinterpret_cast<double *>(reinterpret_cast<uint8_t *>(outbuf) + plan.out_bytes());
-    uint64_t *full = reinterpret_cast<uint64_t *>(csums + WS_CWARPS * G * 2);
+    uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(outbuf) + plan.out_bytes());
     uint64_t *empty = full + S;
     uint64_t *posbar = empty + S;
     __shared__ volatile int s_abort;
@@ -520,19 +515,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
     const int cpw = (SC_T + wph - 1) / wph;              /* cells of a tile per warp */
     const float inv17 = 1.0f / 17.0f;
     float *ob = outbuf + warp * G * SC_T;                /* [g][cell] */
-    double *csw = csums + warp * G * 2;
-    if (lane < G) { csw[2 * lane] = 0.0; csw[2 * lane + 1] = 0.0; }
     f2_t qr[G][QPL], qi[G][QPL], qx[G][QPL];
-    int cur_l = -1, cur_chunk = -1, chunk_u = 0;
-    auto flush = [&]() {
-        if (cur_chunk >= 0 && active && lane < G) {
-            double *cs = a.csum + (((int64_t)chunk_u * G + lane) * a.n_chunks + cur_chunk) * 2;
-            atomicAdd(cs, csw[2 * lane]);
-            atomicAdd(cs + 1, csw[2 * lane + 1]);
-            csw[2 * lane] = 0.0;
-            csw[2 * lane + 1] = 0.0;
-        }
-    };
+    int cur_l = -1;
 
     for (int k = 0; k < n_mine; k++) {
         const int st = k % S;
@@ -565,12 +549,6 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                         qi[g][i] = pk(m.x * inv17, m.y * inv17);
                         qx[g][i] = *reinterpret_cast<const f2_t *>(src + g * 3 * FC + 2 * FC + 2 * q);
                     }
-            }
-            const int chunk = c0 / ZN_CHUNK_ROWS;
-            if (chunk != cur_chunk || u != chunk_u) {
-                flush();
-                cur_chunk = chunk;
-                chunk_u = u;
             }
             const int hoff = h * a.row_bytes;
             for (int cb = cbeg; cb < cend; cb += 4) {
@@ -636,26 +614,15 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                 }
             }
             __syncwarp();
-            /* cells [cbeg, cend): write out, fold into the chunk sums */
+            /* cells [cbeg, cend): write out */
             for (int i = lane; i < G * cpw; i += 32) {
                 const int g = i / cpw, c = cbeg + (i - g * cpw);
                 if (c < cend) a.raw[((int64_t)u * G + g) * a.raw_stride + c0 + c] = ob[g * SC_T + c];
-            }
-            if (lane < G) {
-                double s1 = csw[2 * lane], s2 = csw[2 * lane + 1];
-                for (int c = cbeg; c < cend; c++) {
-                    const double x = ob[lane * SC_T + c];
-                    s1 += x;
-                    s2 += x * x;
-                }
-                csw[2 * lane] = s1;
-                csw[2 * lane + 1] = s2;
             }
             __syncwarp();
         }
         if (lane == 0) mbar_arrive(&empty[st]);
     }
-    flush();
 }
 
 /* ------------------------------------------------------------------ */
@@ -664,52 +631,42 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
 /*
  * triattention.c:228-236 forms mean = fl(sum)/n and var with two sequential
  * fp32 chains  s <- fl(s + v_k).  Summing more accurately would move z by up
- * to ~1e-5 at 32k rows, so the chains are reproduced bit for bit, but in
- * parallel:
+ * to ~1e-5 at 32k rows, so the chains are reproduced bit for bit, but a warp
+ * advances them 512 elements per step:
  *
  * While s and every partial result stay in one binade [2^E, 2^(E+1)), each
  * fp32 add rounds on the fixed grid ulp = 2^(E-23): with s = M*ulp (M the
- * 24-bit significand), fl(s + v) = (M + round(v/ulp))*ulp, ties to even M.
- * So a chunk of adds is an integer translation D of M that depends only on E
- * and on the parity of M (ties).  The CTA predicts E for every chunk from a
- * double prefix sum, builds (D_end, D_min, D_max) per chunk and per parity
- * (phase B, a warp per chunk), then warp 0 walks the chunks (phase C): it
- * applies a chunk's translation only when the running s is really in the
- * predicted binade and M + D stays strictly inside [2^23, 2^24) for every
- * partial sum -- which proves each exact s_k + v_k was inside the binade, so
- * the grid rounding was the fp32 rounding.  Any other chunk (the first ones,
- * binade crossings, NaN/Inf, huge values) is added the sequential way.  The
- * result is identical to the reference's chain for every input; the
- * prediction only decides how many chunks take the slow path.
+ * signed 24-bit significand), fl(s + v) = (M + round(v/ulp))*ulp, ties to
+ * even M.  A step takes E and M from the running s, lets every lane turn its
+ * 16 consecutive elements into integer increments, forms their in-order
+ * prefix sums (lane prefix + warp scan; ties resolved in order by parity),
+ * and accepts the longest prefix whose partial significands stay strictly
+ * inside (2^23, 2^24) -- which proves every exact s_k + v_k lay inside the
+ * binade, so the grid rounding was the fp32 rounding.  The first element that
+ * leaves the binade (or is not finite) is added with one plain fp32 add and
+ * the walk resumes after it.  The result equals the reference's chain for
+ * every input.  One warp walks one chain; its data streams through a small
+ * per-warp ring of bulk copies.  Waits are bounded (ST_TIMEOUT).
  */
 
-constexpr int ZN_THREADS = 128;
-constexpr int ZN_MAXCH = 512;          /* chunks per chain kept in shared memory */
+constexpr int ZW_WARPS = 4;                      /* chains per CTA */
+constexpr int ZW_EPL = 16;                       /* elements per lane per step */
+constexpr int ZW_BLOCK = 32 * ZW_EPL;            /* 512 elements per step / ring slot */
+constexpr int ZW_STAGES = 4;
 
 struct ZArgs {
     const float *raw;
-    int64_t raw_stride;
+    int64_t raw_stride;                  /* floats, multiple of 4 */
     int32_t G, units;
     float2 *ms;                          /* [units*G] (mean, std) */
-    const double *csum;                  /* optional [units*G][n_chunks][2] per-128-row (sum, sum sq) */
-    int32_t n_chunks;
+    int32_t *status;                     /* may be NULL */
     int32_t n_rows[TRIA_MAX_UNITS];
 };
 
-struct ZnShared {
-    double P[ZN_MAXCH];                  /* chunk sums, then prefix sums at chunk starts */
-    int dend[2][ZN_MAXCH], dmin[2][ZN_MAXCH], dmax[2][ZN_MAXCH];
-    short E[ZN_MAXCH];
-    unsigned char ok[ZN_MAXCH];
-    double wsum[ZN_THREADS / 32];
-    float stage[128];                    /* one 128-element piece of a fallback chunk */
-    float result;
-};
-
-/* v/ulp rounded onto the integer grid of binade E (ulp = 2^(E-23)), given the
- * parity of the running significand.  Returns 0 = ok, 1 = tie (d assumes the
- * given parity), 2 = v cannot stay within the binade (or is not finite). */
-__device__ __forceinline__ int grid_delta(float v, int E, int par, int &d) {
+/* v/ulp rounded onto the integer grid of binade E (ulp = 2^(E-23)).  Returns
+ * 0 = ok, 1 = tie (d = the lower candidate), 2 = v cannot stay within the
+ * binade (too large, or not finite). */
+__device__ __forceinline__ int grid_delta(float v, int E, int &d) {
     const uint32_t b = __float_as_uint(v);
     const int exb = (b >> 23) & 0xff;
     if (exb == 255) return 2;
@@ -723,244 +680,194 @@ __device__ __forceinline__ int grid_delta(float v, int E, int par, int &d) {
     const int fl = Q >> sh;                             /* floor */
     const int r = Q & ((1 << sh) - 1);
     const int half = 1 << (sh - 1);
-    if (r < half) { d = fl; return 0; }
-    if (r > half) { d = fl + 1; return 0; }
-    d = ((par + fl) & 1) ? fl + 1 : fl;                 /* tie: even significand */
-    return 1;
+    d = r > half ? fl + 1 : fl;
+    return r == half ? 1 : 0;
 }
 
-__device__ __forceinline__ double warp_sum_d(double v) {
+/* v[idx] of register array v with a runtime idx, without spilling v. */
+template <int N>
+__device__ __forceinline__ float pick(const float (&v)[N], int idx) {
+    float r = v[0];
 #pragma unroll
-    for (int m = 16; m; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
-    return v;
-}
-
-/* Four consecutive elements [k, k+4) of x (k % 4 == 0); `cnt` of them exist. */
-__device__ __forceinline__ float4 load4(const float *__restrict__ x, int k, int n, int &cnt) {
-    cnt = max(0, min(4, n - k));
-    if (cnt == 4) return __ldcg(reinterpret_cast<const float4 *>(x + k));
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (cnt > 0) v.x = x[k];
-    if (cnt > 1) v.y = x[k + 1];
-    if (cnt > 2) v.z = x[k + 2];
-    return v;
-}
-
-/* The fp32 sequential sum of val(x[0..n)) (val = identity for the mean, the
- * reference's fl(fl(x-mean)^2) for the variance).  x is 16-byte aligned; a
- * chunk is M = 128*P elements, P pieces of one float4 per lane.  When
- * have_sums, sh.P already holds the chunk sums (they only steer the binade
- * guess).  Result valid in all threads. */
-template <class Val>
-__device__ float exact_chain_sum(const float *__restrict__ x, int n, int M, int nch, ZnShared &sh, Val val,
-                                 bool have_sums) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    constexpr int NW = ZN_THREADS / 32;
-    const int P = M / 128;
-
-    /* A: chunk sums in double */
-    for (int j = have_sums ? nch : warp; j < nch; j += NW) {
-        const int b = j * M;
-        double acc = 0.0;
-        for (int pc = 0; pc < P; pc++) {
-            int c;
-            const float4 v = load4(x, b + 128 * pc + 4 * lane, n, c);
-            if (c > 0) acc += (double)val(v.x);
-            if (c > 1) acc += (double)val(v.y);
-            if (c > 2) acc += (double)val(v.z);
-            if (c > 3) acc += (double)val(v.w);
-        }
-        acc = warp_sum_d(acc);
-        if (lane == 0) sh.P[j] = acc;
-    }
-    __syncthreads();
-    {   /* exclusive prefix in chunk order */
-        const int cpt = (nch + ZN_THREADS - 1) / ZN_THREADS;
-        const int j0 = min(tid * cpt, nch), j1 = min(j0 + cpt, nch);
-        double loc = 0.0;
-        for (int j = j0; j < j1; j++) loc += sh.P[j];
-        double inc = loc;
-#pragma unroll
-        for (int m = 1; m < 32; m <<= 1) {
-            const double t = __shfl_up_sync(0xffffffffu, inc, m);
-            if (lane >= m) inc += t;
-        }
-        if (lane == 31) sh.wsum[warp] = inc;
-        __syncthreads();
-        double base = inc - loc;
-        for (int w = 0; w < warp; w++) base += sh.wsum[w];
-        for (int j = j0; j < j1; j++) { const double t = sh.P[j]; sh.P[j] = base; base += t; }
-    }
-    __syncthreads();
-
-    /* B: per-chunk translations (a warp per chunk, pieces in element order) */
-    for (int j = warp; j < nch; j += NW) {
-        const int b = j * M, e = min(b + M, n);
-        const double pj = sh.P[j];
-        int E = 0;
-        bool valid = false;
-        if (pj != 0.0) {
-            const int exd = (__double2hiint(pj) >> 20) & 0x7ff;
-            E = exd - 1023;
-            valid = exd != 0x7ff && E >= -126 && E <= 127;
-        }
-        if (!valid) { if (lane == 0) sh.ok[j] = 0; continue; }
-        int run = 0, gmin = INT_MAX, gmax = INT_MIN;
-        bool bad = false, tie = false;
-        for (int pc = 0; pc < P; pc++) {
-            int c0;
-            const float4 v0 = load4(x, b + 128 * pc + 4 * lane, n, c0);
-            const float vv[4] = {v0.x, v0.y, v0.z, v0.w};
-            int dsum = 0, lmin = INT_MAX, lmax = INT_MIN;
-#pragma unroll
-            for (int t = 0; t < 4; t++) {
-                if (t < c0) {
-                    int d = 0;
-                    const int st = grid_delta(val(vv[t]), E, 0, d);
-                    bad |= st == 2;
-                    tie |= st == 1;
-                    dsum += d;
-                    lmin = min(lmin, dsum);
-                    lmax = max(lmax, dsum);
-                }
-            }
-            if (dsum > (1 << 23) || dsum < -(1 << 23)) bad = true;
-            int inc = dsum;
-#pragma unroll
-            for (int m = 1; m < 32; m <<= 1) {
-                const int t = __shfl_up_sync(0xffffffffu, inc, m);
-                if (lane >= m) inc += t;
-            }
-            const int off = run + inc - dsum;
-            if (lmin != INT_MAX) { gmin = min(gmin, lmin + off); gmax = max(gmax, lmax + off); }
-            run += __shfl_sync(0xffffffffu, inc, 31);
-            if (run > (1 << 23) || run < -(1 << 23)) bad = true;
-        }
-        if (__any_sync(0xffffffffu, bad)) { if (lane == 0) sh.ok[j] = 0; continue; }
-        if (!__any_sync(0xffffffffu, tie)) {
-#pragma unroll
-            for (int m = 16; m; m >>= 1) {
-                gmin = min(gmin, __shfl_xor_sync(0xffffffffu, gmin, m));
-                gmax = max(gmax, __shfl_xor_sync(0xffffffffu, gmax, m));
-            }
-            if (lane == 0) {
-                const bool fits = gmin >= -(1 << 23) && gmax <= (1 << 23);
-                for (int p = 0; p < 2; p++) { sh.dend[p][j] = run; sh.dmin[p][j] = gmin; sh.dmax[p][j] = gmax; }
-                sh.E[j] = (short)E;
-                sh.ok[j] = fits ? 1 : 0;
-            }
-        } else if (lane == 0) {                          /* ties: the parity path matters */
-            bool fits = true;
-            for (int p = 0; p < 2 && fits; p++) {
-                int D = 0, mn = INT_MAX, mx = INT_MIN;
-                for (int k = b; k < e && fits; k++) {
-                    int d = 0;
-                    if (grid_delta(val(x[k]), E, (p + D) & 1, d) == 2) fits = false;
-                    D += d;
-                    mn = min(mn, D);
-                    mx = max(mx, D);
-                    if (D > (1 << 23) || D < -(1 << 23)) fits = false;
-                }
-                sh.dend[p][j] = D; sh.dmin[p][j] = mn; sh.dmax[p][j] = mx;
-            }
-            sh.E[j] = (short)E;
-            sh.ok[j] = fits ? 1 : 0;
-        }
-    }
-    __syncthreads();
-
-    /* C: warp 0 walks the chunks (all lanes in step, same values); a chunk
-     * that cannot be translated is staged through shared memory, 128
-     * elements at a time, and added sequentially. */
-    if (warp == 0) {
-        float s = 0.f;
-        for (int j = 0; j < nch; j++) {
-            bool done = false;
-            if (sh.ok[j]) {
-                const uint32_t bits = __float_as_uint(s);
-                const int exb = (bits >> 23) & 0xff;
-                if (exb != 0 && exb != 255 && exb - 127 == sh.E[j]) {
-                    const int mabs = (int)((bits & 0x7fffffu) | 0x800000u);
-                    const int p = mabs & 1;
-                    const bool neg = bits >> 31;
-                    const int ms = neg ? -mabs : mabs;
-                    const int lo = ms + sh.dmin[p][j], hi = ms + sh.dmax[p][j];
-                    const bool in = neg ? (hi <= -((1 << 23) + 1) && lo >= -((1 << 24) - 1))
-                                        : (lo >= (1 << 23) + 1 && hi <= (1 << 24) - 1);
-                    if (in) {
-                        const int mn = ms + sh.dend[p][j];
-                        const uint32_t a = (uint32_t)(neg ? -mn : mn);
-                        s = __uint_as_float((bits & 0x80000000u) | ((uint32_t)exb << 23) | (a & 0x7fffffu));
-                        done = true;
-                    }
-                }
-            }
-            if (!done) {
-                const int b = j * M, e = min(b + M, n);
-                for (int pb = b; pb < e; pb += 128) {
-                    int c;
-                    const float4 v = load4(x, pb + 4 * lane, n, c);
-                    __syncwarp();
-                    if (c > 0) sh.stage[4 * lane] = v.x;
-                    if (c > 1) sh.stage[4 * lane + 1] = v.y;
-                    if (c > 2) sh.stage[4 * lane + 2] = v.z;
-                    if (c > 3) sh.stage[4 * lane + 3] = v.w;
-                    __syncwarp();
-                    const int cnt = min(128, e - pb);
-#pragma unroll 8
-                    for (int k = 0; k < cnt; k++) s = __fadd_rn(s, val(sh.stage[k]));
-                }
-            }
-        }
-        if (lane == 0) sh.result = s;
-    }
-    __syncthreads();
-    const float r = sh.result;
-    __syncthreads();
+    for (int t = 1; t < N; t++) r = t == idx ? v[t] : r;
     return r;
 }
 
-/* One CTA per (unit, query head) chain: (mean, std) of triattention.c:227-238. */
-__global__ void __launch_bounds__(ZN_THREADS) k_znorm_exact(const ZArgs a) {
-    __shared__ ZnShared sh;
-    const int t = blockIdx.x;
-    if (t >= a.units * a.G) return;
+struct ZwShared {
+    float ring[ZW_WARPS][ZW_STAGES][ZW_BLOCK];
+    uint64_t bar[ZW_WARPS][ZW_STAGES];
+};
+
+/* One warp: the fp32 sequential sum of val(x[0..n)), reading ring blocks
+ * [blk0, blk0 + nb) of its stream (block b of the stream = data block
+ * b % nb).  `issue(b)` requests stream block b.  Returns the sum (all lanes). */
+template <class Val, class Issue>
+__device__ float walk_chain(const float *ring_base, uint64_t *bars, int n, int nb, int blk0, int total_blocks,
+                            Val val, Issue issue, int32_t *status, bool &aborted) {
+    const int lane = threadIdx.x & 31;
+    float s = 0.f;
+    for (int bi = 0; bi < nb; bi++) {
+        const int g = blk0 + bi;                        /* stream block */
+        const int st = g % ZW_STAGES;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars[st], (uint32_t)((g / ZW_STAGES) & 1)))) {
+            if (lane == 0 && status) atomicOr(status, ST_TIMEOUT);
+            aborted = true;
+            return __int_as_float(0x7fc00000);          /* NaN: the status says why */
+        }
+        const float *blk = ring_base + st * ZW_BLOCK;
+        const int base = bi * ZW_BLOCK;
+        const int cnt = min(ZW_BLOCK, n - base);
+        float v[ZW_EPL];
+#pragma unroll
+        for (int t = 0; t < ZW_EPL; t += 4) {
+            const float4 w = *reinterpret_cast<const float4 *>(blk + lane * ZW_EPL + t);
+            v[t] = val(w.x); v[t + 1] = val(w.y); v[t + 2] = val(w.z); v[t + 3] = val(w.w);
+        }
+        int p = 0;                                      /* first element of the block not yet added */
+        while (p < cnt) {
+            const uint32_t bits = __float_as_uint(s);
+            const int exb = (bits >> 23) & 0xff;
+            if (exb == 0 || exb == 255) {               /* s zero / subnormal / not finite: one plain add */
+                s = __fadd_rn(s, __shfl_sync(0xffffffffu, pick(v, p % ZW_EPL), p / ZW_EPL));
+                p++;
+                continue;
+            }
+            const int E = exb - 127;
+            const int mabs = (int)((bits & 0x7fffffu) | 0x800000u);
+            const int M = (bits >> 31) ? -mabs : mabs;
+            /* increments of this lane's elements (elements before p or past cnt: 0) */
+            int d[ZW_EPL];
+            unsigned tie = 0, bad = 0;
+            int lsum = 0;
+#pragma unroll
+            for (int t = 0; t < ZW_EPL; t++) {
+                const int e = lane * ZW_EPL + t;
+                int dd = 0;
+                if (e >= p && e < cnt) {
+                    const int st = grid_delta(v[t], E, dd);
+                    if (st == 1) tie |= 1u << t;
+                    if (st == 2) bad |= 1u << t;
+                }
+                d[t] = dd;
+                lsum += dd;
+            }
+            /* exclusive warp scan of the lane totals (ints; |lsum| < 2^29) */
+            int inc = lsum;
+#pragma unroll
+            for (int m = 1; m < 32; m <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, inc, m);
+                if (lane >= m) inc += y;
+            }
+            int off = inc - lsum;                       /* sum of increments of earlier lanes */
+            /* ties in element order: the candidate with an even significand */
+            unsigned tmask = __ballot_sync(0xffffffffu, tie != 0);
+            while (tmask) {
+                const int tl = __ffs(tmask) - 1;
+                int adj = 0, tt = 0;
+                if (lane == tl) {
+                    tt = __ffs(tie) - 1;
+                    int before = off;
+#pragma unroll
+                    for (int t = 0; t < ZW_EPL; t++) if (t < tt) before += d[t];
+                    /* candidates M+before+d and +1: keep the even one */
+                    adj = ((M + before + d[tt]) & 1) ? 1 : 0;
+                    tie &= ~(1u << tt);
+                }
+                adj = __shfl_sync(0xffffffffu, adj, tl);
+                tt = __shfl_sync(0xffffffffu, tt, tl);
+                if (lane == tl) {
+#pragma unroll
+                    for (int t = 0; t < ZW_EPL; t++) if (t == tt) d[t] += adj;
+                } else if (lane > tl) {
+                    off += adj;
+                }
+                tmask = __ballot_sync(0xffffffffu, tie != 0);
+            }
+            /* first element whose partial significand leaves the open binade */
+            int first_bad = ZW_BLOCK;
+            {
+                int run = M + off;
+#pragma unroll
+                for (int t = 0; t < ZW_EPL; t++) {
+                    const int e = lane * ZW_EPL + t;
+                    run += d[t];
+                    const bool live = e >= p && e < cnt;
+                    const bool out = (bad >> t) & 1 ||
+                                     (M > 0 ? (run <= (1 << 23) || run >= (1 << 24))
+                                            : (run >= -(1 << 23) || run <= -(1 << 24)));
+                    if (live && out && first_bad == ZW_BLOCK) first_bad = e;
+                }
+            }
+#pragma unroll
+            for (int m = 16; m; m >>= 1) first_bad = min(first_bad, __shfl_xor_sync(0xffffffffu, first_bad, m));
+            const int stop = min(first_bad, cnt);       /* elements [p, stop) are exact translations */
+            if (stop > p) {
+                /* M + (increments of elements < stop): from the lane that holds element stop-1 */
+                const int hl = (stop - 1) / ZW_EPL, ht = (stop - 1) % ZW_EPL;
+                int part = M + off;
+#pragma unroll
+                for (int t = 0; t < ZW_EPL; t++) if (t <= ht) part += d[t];
+                part = __shfl_sync(0xffffffffu, part, hl);
+                const uint32_t a = (uint32_t)(part < 0 ? -part : part);
+                s = __uint_as_float((bits & 0x80000000u) | ((uint32_t)exb << 23) | (a & 0x7fffffu));
+            }
+            p = stop;
+            if (p < cnt) {                              /* the element that left the binade */
+                s = __fadd_rn(s, __shfl_sync(0xffffffffu, pick(v, p % ZW_EPL), p / ZW_EPL));
+                p++;
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && g + ZW_STAGES < total_blocks) issue(g + ZW_STAGES);
+    }
+    return s;
+}
+
+/* One warp per (unit, query head) chain: (mean, std) of triattention.c:227-238. */
+__global__ void __launch_bounds__(ZW_WARPS * 32) k_znorm_walk(const ZArgs a) {
+    __shared__ ZwShared sh;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * ZW_WARPS + warp;
+    const bool live = t < a.units * a.G;
+    if (lane == 0)
+        for (int i = 0; i < ZW_STAGES; i++) mbar_init(&sh.bar[warp][i], 1);
+    if (threadIdx.x == 0) asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncthreads();
+    if (!live) return;
     const int n = a.n_rows[t / a.G];
     const float *x = a.raw + (int64_t)t * a.raw_stride;
-    int M = 128;
-    while ((n + M - 1) / M > ZN_MAXCH) M *= 2;
-    const int nch = (n + M - 1) / M;
-    /* predictor sums from the scoring kernel when it produced them */
-    const bool pre = a.csum != nullptr;
-    const double *cs = pre ? a.csum + (int64_t)t * a.n_chunks * 2 : nullptr;
-    const int per = M / ZN_CHUNK_ROWS;
-    if (pre) {
-        for (int j = threadIdx.x; j < nch; j += ZN_THREADS) {
-            double s1 = 0.0;
-            for (int i = j * per; i < min((j + 1) * per, a.n_chunks); i++) s1 += cs[2 * i];
-            sh.P[j] = s1;
-        }
-        __syncthreads();
-    }
-    const float sum = exact_chain_sum(x, n, M, nch, sh, [](float v) { return v; }, pre);
+    const int nb = (n + ZW_BLOCK - 1) / ZW_BLOCK;
+    const int total = 2 * nb;                             /* the data twice: mean, then variance */
+    float *ring = &sh.ring[warp][0][0];
+    uint64_t *bars = sh.bar[warp];
+    int issued = 0;                                       /* lane 0's count of requested blocks */
+    auto issue = [&](int g) {                             /* lane 0: stream block g -> its slot */
+        const int b = g % nb;
+        const int st = g % ZW_STAGES;
+        const int cnt = min(ZW_BLOCK, n - b * ZW_BLOCK);
+        const uint32_t bytes = (uint32_t)((cnt + 3) / 4 * 16);   /* within the row: stride % 4 == 0 */
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive_tx(&bars[st], bytes);
+        bulk_g2s(ring + st * ZW_BLOCK, x + (int64_t)b * ZW_BLOCK, bytes, &bars[st]);
+        issued = g + 1;
+    };
+    if (lane == 0)
+        for (int g = 0; g < min(ZW_STAGES, total); g++) issue(g);
+    __syncwarp();
+    bool aborted = false;
+    const float sum = walk_chain(ring, bars, n, nb, 0, total, [](float v) { return v; }, issue, a.status, aborted);
     const float mean = __fdiv_rn(sum, (float)n);
-    if (pre) {
-        const double m = mean;
-        for (int j = threadIdx.x; j < nch; j += ZN_THREADS) {
-            double s = 0.0;
-            for (int i = j * per; i < min((j + 1) * per, a.n_chunks); i++) {
-                const double cnt = (double)max(0, min(ZN_CHUNK_ROWS, n - i * ZN_CHUNK_ROWS));
-                s += cs[2 * i + 1] - 2.0 * m * cs[2 * i] + cnt * m * m;
-            }
-            sh.P[j] = s;
-        }
-        __syncthreads();
-    }
-    const float var = exact_chain_sum(x, n, M, nch, sh, [mean](float v) {
+    const float var = aborted ? sum : walk_chain(ring, bars, n, nb, nb, total, [mean](float v) {
         const float d = __fsub_rn(v, mean);
         return __fmul_rn(d, d);
-    }, pre);
-    if (threadIdx.x == 0) {
+    }, issue, a.status, aborted);
+    if (aborted) {                                        /* copies still in flight must land first */
+        if (lane == 0)
+            for (int g = max(0, issued - ZW_STAGES); g < issued; g++)
+                mbar_wait(&bars[g % ZW_STAGES], (uint32_t)((g / ZW_STAGES) & 1));
+        __syncwarp();
+    }
+    if (lane == 0) {
         float sd = __fsqrt_rn(__fdiv_rn(var, (float)n));
         if (sd < 1e-6f) sd = 1e-6f;
         a.ms[t] = make_float2(mean, sd);
