@@ -644,15 +644,22 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
  * inside (2^23, 2^24) -- which proves every exact s_k + v_k lay inside the
  * binade, so the grid rounding was the fp32 rounding.  The first element that
  * leaves the binade (or is not finite) is added with one plain fp32 add and
- * the walk resumes after it.  The result equals the reference's chain for
- * every input.  One warp walks one chain; its data streams through a small
- * per-warp ring of bulk copies.  Waits are bounded (ST_TIMEOUT).
+ * the walk resumes after it.  The common step (no tie, no exit) is decided
+ * from each lane's prefix extremes and one vote.  When a block needs more
+ * than ZW_WALK_STEPS steps -- s is small next to its elements, as near the
+ * start of a chain or where a zero-mean sum wanders near 0 -- one lane adds
+ * the rest of the block with plain fp32 adds from shared memory (4 cycles an
+ * element), which beats a 512-wide step per binade exit.  The result equals
+ * the reference's chain for every input.  One warp walks one chain; its data
+ * streams through a per-warp ring of bulk copies.  Waits are bounded
+ * (ST_TIMEOUT).
  */
 
 constexpr int ZW_WARPS = 4;                      /* chains per CTA */
 constexpr int ZW_EPL = 16;                       /* elements per lane per step */
 constexpr int ZW_BLOCK = 32 * ZW_EPL;            /* 512 elements per step / ring slot */
-constexpr int ZW_STAGES = 4;
+constexpr int ZW_STAGES = 8;                     /* 16 KB of copies in flight per chain */
+constexpr int ZW_WALK_STEPS = 2;                 /* walk steps per block before plain adds */
 
 struct ZArgs {
     const float *raw;
@@ -662,27 +669,6 @@ struct ZArgs {
     int32_t *status;                     /* may be NULL */
     int32_t n_rows[TRIA_MAX_UNITS];
 };
-
-/* v/ulp rounded onto the integer grid of binade E (ulp = 2^(E-23)).  Returns
- * 0 = ok, 1 = tie (d = the lower candidate), 2 = v cannot stay within the
- * binade (too large, or not finite). */
-__device__ __forceinline__ int grid_delta(float v, int E, int &d) {
-    const uint32_t b = __float_as_uint(v);
-    const int exb = (b >> 23) & 0xff;
-    if (exb == 255) return 2;
-    const int m24 = exb ? (int)((b & 0x7fffffu) | 0x800000u) : (int)(b & 0x7fffffu);
-    const int ex = exb ? exb - 127 : -126;
-    const int sh = E - ex;                              /* v/ulp = +-m24 * 2^-sh */
-    if (sh < 0) return 2;
-    const int Q = (b >> 31) ? -m24 : m24;
-    if (sh == 0) { d = Q; return (Q >= (1 << 23) || Q <= -(1 << 23)) ? 2 : 0; }
-    if (sh >= 25) { d = 0; return 0; }                  /* |v/ulp| < 1/2 */
-    const int fl = Q >> sh;                             /* floor */
-    const int r = Q & ((1 << sh) - 1);
-    const int half = 1 << (sh - 1);
-    d = r > half ? fl + 1 : fl;
-    return r == half ? 1 : 0;
-}
 
 /* v[idx] of register array v with a runtime idx, without spilling v. */
 template <int N>
@@ -724,7 +710,27 @@ __device__ float walk_chain(const float *ring_base, uint64_t *bars, int n, int n
             v[t] = val(w.x); v[t + 1] = val(w.y); v[t + 2] = val(w.z); v[t + 3] = val(w.w);
         }
         int p = 0;                                      /* first element of the block not yet added */
+        int steps = 0;
         while (p < cnt) {
+            if (++steps > ZW_WALK_STEPS) {
+                /* s keeps leaving its binade (it is small next to the elements): the
+                 * rest of the block as plain fp32 adds by one lane, from shared memory */
+                float acc = s;
+                if (lane == 0) {
+                    int e = p;
+                    for (; e < cnt && (e & 3); e++) acc = __fadd_rn(acc, val(blk[e]));
+                    for (; e + 4 <= cnt; e += 4) {
+                        const float4 w = *reinterpret_cast<const float4 *>(blk + e);
+                        acc = __fadd_rn(acc, val(w.x));
+                        acc = __fadd_rn(acc, val(w.y));
+                        acc = __fadd_rn(acc, val(w.z));
+                        acc = __fadd_rn(acc, val(w.w));
+                    }
+                    for (; e < cnt; e++) acc = __fadd_rn(acc, val(blk[e]));
+                }
+                s = __shfl_sync(0xffffffffu, acc, 0);
+                break;
+            }
             const uint32_t bits = __float_as_uint(s);
             const int exb = (bits >> 23) & 0xff;
             if (exb == 0 || exb == 255) {               /* s zero / subnormal / not finite: one plain add */
@@ -733,44 +739,84 @@ __device__ float walk_chain(const float *ring_base, uint64_t *bars, int n, int n
                 continue;
             }
             const int E = exb - 127;
+            if (E < -104) {                             /* s so small that 2^(23-E) is not a float */
+                s = __fadd_rn(s, __shfl_sync(0xffffffffu, pick(v, p % ZW_EPL), p / ZW_EPL));
+                p++;
+                continue;
+            }
             const int mabs = (int)((bits & 0x7fffffu) | 0x800000u);
             const int M = (bits >> 31) ? -mabs : mabs;
-            /* increments of this lane's elements (elements before p or past cnt: 0) */
-            int d[ZW_EPL];
+            /* live elements of this lane: [p, cnt) within [16*lane, 16*lane+16) */
+            const int lo = max(0, p - lane * ZW_EPL), hi = min(ZW_EPL, cnt - lane * ZW_EPL);
+            const unsigned live = hi > lo ? (((hi >= 32 ? 0u : (1u << hi)) - 1u) & ~((1u << lo) - 1u)) : 0u;
+            /* increments v/ulp rounded to the grid: q = v * 2^(23-E) is exact while
+             * |v| < 2^(E+1); ties keep the lower candidate and are settled below */
+            const float scale = __int_as_float((150 - E) << 23);
+            const uint32_t lim = (uint32_t)(E + 128) << 23;          /* bits of 2^(E+1) */
+            /* increments and their sums are kept modulo 2^32: every value that is used
+             * (partials inside the binade) is < 2^24 in magnitude, so wrap-around of
+             * discarded ones does no harm */
+            uint32_t d[ZW_EPL];
             unsigned tie = 0, bad = 0;
-            int lsum = 0;
+            uint32_t lsum = 0;
+            int pmin = INT_MAX, pmax = INT_MIN;         /* extremes of this lane's live prefix sums */
 #pragma unroll
             for (int t = 0; t < ZW_EPL; t++) {
-                const int e = lane * ZW_EPL + t;
-                int dd = 0;
-                if (e >= p && e < cnt) {
-                    const int st = grid_delta(v[t], E, dd);
-                    if (st == 1) tie |= 1u << t;
-                    if (st == 2) bad |= 1u << t;
-                }
+                const float q = v[t] * scale;
+                const float r = rintf(q);
+                const bool isb = (__float_as_uint(v[t]) & 0x7fffffffu) >= lim;
+                const bool ist = fabsf(q - r) == 0.5f;
+                uint32_t dd = (uint32_t)(ist ? (int)(q - 0.5f) : __float2int_rn(r));
+                const bool on = (live >> t) & 1;
+                dd = (on && !isb) ? dd : 0u;
+                tie |= (on && ist && !isb ? 1u : 0u) << t;
+                bad |= (on && isb ? 1u : 0u) << t;
                 d[t] = dd;
                 lsum += dd;
+                /* |increment| <= 2^24, so a lane's prefix sums fit an int */
+                pmin = on ? min(pmin, (int)lsum) : pmin;
+                pmax = on ? max(pmax, (int)lsum) : pmax;
             }
-            /* exclusive warp scan of the lane totals (ints; |lsum| < 2^29) */
-            int inc = lsum;
+            /* exclusive warp scan of the lane totals */
+            uint32_t inc = lsum;
 #pragma unroll
             for (int m = 1; m < 32; m <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, inc, m);
+                const uint32_t y = __shfl_up_sync(0xffffffffu, inc, m);
                 if (lane >= m) inc += y;
             }
-            int off = inc - lsum;                       /* sum of increments of earlier lanes */
+            uint32_t off = inc - lsum;                       /* sum of increments of earlier lanes */
+            /* Whole step at once when no live element is a tie or out of the binade
+             * and both extremes of every lane's partial significands lie inside
+             * [2^23 + 1, 2^24 - 1] (then all of them do).  A lane whose earlier
+             * lanes all pass has an exact `off`; the first failing lane therefore
+             * sees true values and fails, so wrap-around cannot pass a bad step. */
+            {
+                const uint32_t sg = M > 0 ? 1u : 0xffffffffu;
+                const uint32_t b0 = (uint32_t)M + off;
+                const bool in_lo = ((b0 + (uint32_t)pmin) * sg - ((1u << 23) + 1u)) <= (1u << 23) - 2u;
+                const bool in_hi = ((b0 + (uint32_t)pmax) * sg - ((1u << 23) + 1u)) <= (1u << 23) - 2u;
+                const bool ok = tie == 0 && bad == 0 && (pmin > pmax || (in_lo && in_hi));
+                if (__all_sync(0xffffffffu, ok)) {
+                    const uint32_t part = __shfl_sync(0xffffffffu, (uint32_t)M + inc, 31);
+                    const uint32_t a = M > 0 ? part : 0u - part;
+                    s = __uint_as_float((bits & 0x80000000u) | ((uint32_t)exb << 23) | (a & 0x7fffffu));
+                    p = cnt;
+                    continue;
+                }
+            }
             /* ties in element order: the candidate with an even significand */
             unsigned tmask = __ballot_sync(0xffffffffu, tie != 0);
             while (tmask) {
                 const int tl = __ffs(tmask) - 1;
-                int adj = 0, tt = 0;
+                uint32_t adj = 0;
+                int tt = 0;
                 if (lane == tl) {
                     tt = __ffs(tie) - 1;
-                    int before = off;
+                    uint32_t upto = off;                     /* increments up to and including tt */
 #pragma unroll
-                    for (int t = 0; t < ZW_EPL; t++) if (t < tt) before += d[t];
-                    /* candidates M+before+d and +1: keep the even one */
-                    adj = ((M + before + d[tt]) & 1) ? 1 : 0;
+                    for (int t = 0; t < ZW_EPL; t++) if (t <= tt) upto += d[t];
+                    /* candidates M+upto (lower) and M+upto+1: keep the even one */
+                    adj = ((uint32_t)M + upto) & 1u;
                     tie &= ~(1u << tt);
                 }
                 adj = __shfl_sync(0xffffffffu, adj, tl);
@@ -786,17 +832,17 @@ __device__ float walk_chain(const float *ring_base, uint64_t *bars, int n, int n
             /* first element whose partial significand leaves the open binade */
             int first_bad = ZW_BLOCK;
             {
-                int run = M + off;
+                /* |run| must stay in [2^23 + 1, 2^24 - 1]; work on the magnitude */
+                const uint32_t sg = M > 0 ? 1u : 0xffffffffu;
+                uint32_t run = ((uint32_t)M + off) * sg;
+                unsigned outm = bad;
 #pragma unroll
                 for (int t = 0; t < ZW_EPL; t++) {
-                    const int e = lane * ZW_EPL + t;
-                    run += d[t];
-                    const bool live = e >= p && e < cnt;
-                    const bool out = (bad >> t) & 1 ||
-                                     (M > 0 ? (run <= (1 << 23) || run >= (1 << 24))
-                                            : (run >= -(1 << 23) || run <= -(1 << 24)));
-                    if (live && out && first_bad == ZW_BLOCK) first_bad = e;
+                    run += d[t] * sg;
+                    outm |= (run - ((1u << 23) + 1u) > (1u << 23) - 2u ? 1u : 0u) << t;
                 }
+                outm &= live;
+                if (outm) first_bad = lane * ZW_EPL + __ffs(outm) - 1;
             }
 #pragma unroll
             for (int m = 16; m; m >>= 1) first_bad = min(first_bad, __shfl_xor_sync(0xffffffffu, first_bad, m));
@@ -804,11 +850,11 @@ __device__ float walk_chain(const float *ring_base, uint64_t *bars, int n, int n
             if (stop > p) {
                 /* M + (increments of elements < stop): from the lane that holds element stop-1 */
                 const int hl = (stop - 1) / ZW_EPL, ht = (stop - 1) % ZW_EPL;
-                int part = M + off;
+                uint32_t part = (uint32_t)M + off;
 #pragma unroll
                 for (int t = 0; t < ZW_EPL; t++) if (t <= ht) part += d[t];
                 part = __shfl_sync(0xffffffffu, part, hl);
-                const uint32_t a = (uint32_t)(part < 0 ? -part : part);
+                const uint32_t a = M > 0 ? part : 0u - part;
                 s = __uint_as_float((bits & 0x80000000u) | ((uint32_t)exb << 23) | (a & 0x7fffffu));
             }
             p = stop;
@@ -824,8 +870,9 @@ __device__ float walk_chain(const float *ring_base, uint64_t *bars, int n, int n
 }
 
 /* One warp per (unit, query head) chain: (mean, std) of triattention.c:227-238. */
-__global__ void __launch_bounds__(ZW_WARPS * 32) k_znorm_walk(const ZArgs a) {
-    __shared__ ZwShared sh;
+__global__ void __launch_bounds__(ZW_WARPS * 32, 1) k_znorm_walk(const ZArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    ZwShared &sh = *reinterpret_cast<ZwShared *>(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * ZW_WARPS + warp;
     const bool live = t < a.units * a.G;
