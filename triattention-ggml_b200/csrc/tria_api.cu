@@ -442,6 +442,16 @@ static WsPlan ws_plan(const tria_ctx *c, const tria_kv_view *v) {
 template <int KT, int G>
 static int launch_ws_inst(const TmaScoreArgs &a, const WsPlan &plan, int grid, cudaStream_t st) {
     auto fn = k_score_ws<KT, G>;
+    /* the setmaxnreg split inside the kernel assumes this launch allocation */
+    static int regs = -1;
+    if (regs < 0) {
+        cudaFuncAttributes fa;
+        CUDA_TRY(cudaFuncGetAttributes(&fa, fn));
+        regs = fa.numRegs;
+    }
+    if (regs != WS_LAUNCH_REGS)
+        FAIL(TRIA_ERR_UNSUPPORTED, "k_score_ws: compiled with %d registers per thread, its register split needs %d",
+             regs, WS_LAUNCH_REGS);
     const int smem = plan.total(64);
     CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     fn<<<grid, WS_THREADS, smem, st>>>(a, plan);

@@ -54,6 +54,15 @@ constexpr int SELECT_THREADS = 1024;
 /* Delta table                                                          */
 /* ------------------------------------------------------------------ */
 
+/* A table row holds one 16-byte chunk (C_2s, C_2s+1, S_2s, S_2s+1) per pair of
+ * frequencies s.  Within each aligned group of four chunks (owned by one lane
+ * of the scoring kernel, group index j = s / 4) the chunks are rotated by
+ * j / 2, so the eight lanes of a cell reading "their" chunk i hit eight
+ * different bank groups.  tab_chunk(s) is the stored position of chunk s. */
+__host__ __device__ __forceinline__ int tab_chunk(int s) {
+    return (s & ~3) | (((s & 3) + ((s >> 3) & 3)) & 3);
+}
+
 __global__ void k_build_table(float2 *__restrict__ T, int64_t d_lo, int64_t n_d,
                               const float *__restrict__ omega, int fc) {
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -72,8 +81,8 @@ __global__ void k_build_table(float2 *__restrict__ T, int64_t d_lo, int64_t n_d,
         c += cd;
         s += sd;
     }
-    /* layout per frequency pair p = f/2: float4 (C_2p, C_2p+1, S_2p, S_2p+1) */
-    float *Tf = reinterpret_cast<float *>(T) + di * 2 * fc + 4 * (f >> 1) + (f & 1);
+    /* chunk s = f/2 holds float4 (C_2s, C_2s+1, S_2s, S_2s+1), stored at tab_chunk(s) */
+    float *Tf = reinterpret_cast<float *>(T) + di * 2 * fc + 4 * tab_chunk(f >> 1) + (f & 1);
     Tf[0] = (float)c;
     Tf[2] = (float)s;
 }
@@ -197,13 +206,13 @@ __global__ void __launch_bounds__(SCORE_THREADS) k_score_raw(const ScoreArgs a) 
                 } else {
                     float kr[FPL], ki[FPL];
                     load_pairs<KT, FPL>(a, kbase + (int64_t)c * a.cell_stride, c, j * FPL, kr, ki);
-                    const float4 *T4 = reinterpret_cast<const float4 *>(a.table + di * FC + j * FPL);
+                    const float4 *T4 = reinterpret_cast<const float4 *>(a.table + di * FC);
                     float acc[G], ext[G];
 #pragma unroll
                     for (int g = 0; g < G; g++) { acc[g] = 0.f; ext[g] = 0.f; }
 #pragma unroll
                     for (int t2 = 0; t2 < FPL / 2; t2++) {
-                        const float4 cs = T4[t2];      /* (C0, C1, S0, S1) of pairs 2*t2, 2*t2+1 */
+                        const float4 cs = T4[tab_chunk(j * FPL / 2 + t2)];   /* (C0, C1, S0, S1) */
 #pragma unroll
                         for (int e = 0; e < 2; e++) {
                             const int t = 2 * t2 + e;
@@ -243,8 +252,20 @@ __global__ void __launch_bounds__(SCORE_THREADS) k_score_raw(const ScoreArgs a) 
 constexpr int ST_TIMEOUT = 2;          /* status bit: a pipeline wait gave up */
 constexpr int SC_T = 16;               /* cells per work item (tile) */
 constexpr int WS_CWARPS = 8;           /* consumer warps: one kv head each */
-constexpr int WS_THREADS = (WS_CWARPS + 1) * 32;   /* + one producer warp */
+constexpr int WS_THREADS = (WS_CWARPS + 4) * 32;   /* + a producer warpgroup, one warp of it working */
+/* Register split (setmaxnreg): the CTA is launched with WS_LAUNCH_REGS per
+ * thread (65536 / 384 rounded down to 8); the producer warpgroup gives its
+ * share back and the consumer warpgroups take it.  The shares must sum to at
+ * most the launch total, or the increase would wait forever; the host checks
+ * the compiled register count before every launch. */
+constexpr int WS_LAUNCH_REGS = 168;
+constexpr int WS_PRODUCER_REGS = 56;
+constexpr int WS_CONSUMER_REGS = 224;
+static_assert(4 * 32 * WS_PRODUCER_REGS + WS_CWARPS * 32 * WS_CONSUMER_REGS <= WS_THREADS * WS_LAUNCH_REGS,
+              "register split exceeds the launch allocation");
+static_assert(WS_THREADS * WS_LAUNCH_REGS <= 65536, "launch allocation exceeds the register file");
 constexpr int WS_POS_RING = 8;         /* positions are fetched this many items ahead */
+constexpr int WS_CPL = 4;              /* cells per lane per pass: a warp's 16 cells at once */
 
 struct TmaScoreArgs {
     const uint8_t *k[TRIA_MAX_LAYERS];
@@ -269,10 +290,9 @@ struct WsPlan {
     __host__ __device__ int k_bytes() const { return SC_T * cell_bytes; }
     __host__ __device__ int tab_bytes(int fc) const { return tab_rows * fc * 8; }
     __host__ __device__ int stage_bytes(int fc) const { return k_bytes() + tab_bytes(fc) + pos_ints * 4; }
-    __host__ __device__ int out_bytes() const { return WS_CWARPS * G * SC_T * 4; }
     __host__ __device__ int ring_bytes() const { return WS_POS_RING * pos_ints * 4; }
     __host__ __device__ int total(int fc) const {
-        return stages * stage_bytes(fc) + ring_bytes() + out_bytes() + (2 * stages + WS_POS_RING) * 8;
+        return stages * stage_bytes(fc) + ring_bytes() + (2 * stages + WS_POS_RING) * 8;
     }
 };
 
@@ -333,7 +353,11 @@ __device__ __forceinline__ f2_t mul2(f2_t a, f2_t b) {
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
-__device__ __forceinline__ f2_t neg2(f2_t x) { return x ^ 0x8000000080000000ull; }
+__device__ __forceinline__ f2_t sub2(f2_t a, f2_t b) {
+    f2_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
 /* Two packed halves -> two packed floats. */
 __device__ __forceinline__ f2_t h2_to_f2(uint32_t h) {
     f2_t r;
@@ -374,14 +398,17 @@ __device__ __forceinline__ void row_pair(const uint8_t *row, int q, f2_t &kr, f2
  * completes when all bytes landed.  Few large copies matter: the copy engine
  * streams 32 KB tiles at HBM speed but not sixteen 2 KB pieces.
  *
- * Each consumer warp scores one kv head, four cells per pass: 8 lanes per
- * cell, lane j of cell slot s owning the frequency pairs j + 8*((i + s) & 3),
- * i = 0..3, so each load instruction reads four different 32-byte windows of
- * K (no bank conflicts) and 128 contiguous bytes of each cell's table row.
- * The lane's q-centre terms (pre-scaled by 1/17) and norm terms for its pairs
- * stay in registers for the whole layer; the math runs as packed f32x2 FMAs;
- * the G sums are reduced across the 8 lanes with a transposing butterfly,
- * staged and written per tile.  Every wait is bounded (ST_TIMEOUT).
+ * Each consumer warp scores one kv head, all 16 cells of the tile in one
+ * pass: 8 lanes per cell, lane j owning the frequency pairs 8j..8j+7 (table
+ * chunks 4j..4j+3) and WS_CPL = 4 cells, so a cell's 8 lanes load 128
+ * contiguous bytes of K per instruction and, through the chunk rotation of
+ * tab_chunk(), eight distinct bank groups of its table row.  The lane's
+ * q-centre terms (pre-scaled by 1/17) and norm terms stay in registers for
+ * the whole layer; the math runs as packed f32x2 FMAs; the G sums are
+ * reduced across the 8 lanes with a transposing butterfly and written
+ * straight to the raw-score rows.  The producer warpgroup hands its
+ * registers to the consumers (setmaxnreg).  Every wait is bounded
+ * (ST_TIMEOUT).
  */
 template <int KT, int G>
 __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a, const WsPlan plan) {
@@ -392,8 +419,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
     const int stage_bytes = plan.stage_bytes(FC);
     uint8_t *stages = smem;
     int32_t *ring = reinterpret_cast<int32_t *>(smem + S * stage_bytes);              /* [WS_POS_RING][pos_ints] */
-    float *outbuf = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ring) + plan.ring_bytes());
-    uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(outbuf) + plan.out_bytes());
+    uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(ring) + plan.ring_bytes());
     uint64_t *empty = full + S;
     uint64_t *posbar = empty + S;
     __shared__ volatile int s_abort;
@@ -416,6 +442,13 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         c0 = (it - l * a.tiles_per_layer) * SC_T;
         return max(0, min(SC_T, a.layer_rows[l] - c0));
     };
+
+    if (warp >= WS_CWARPS) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(WS_PRODUCER_REGS));
+        if (warp != WS_CWARPS) return;
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(WS_CONSUMER_REGS));
+    }
 
     if (warp == WS_CWARPS) {
         /* ---------------- producer ---------------- */
@@ -508,28 +541,33 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
     }
 
     /* ---------------- consumers ---------------- */
-    const int j = lane & 7, cs4 = lane >> 3;             /* pair owner, cell of the pass */
+    const int j = lane & 7, cs4 = lane >> 3;             /* chunk group (pairs 8j..8j+7), cell of the pass */
     const int wph = max(1, WS_CWARPS / KV);              /* warps per head */
     const bool active = warp < KV * wph;
     const int h = active ? warp % KV : 0, sub = warp / KV;
     const int cpw = (SC_T + wph - 1) / wph;              /* cells of a tile per warp */
     const float inv17 = 1.0f / 17.0f;
-    float *ob = outbuf + warp * G * SC_T;                /* [g][cell] */
+    int toff[QPL];                                       /* bytes of chunk 4j+i within a table row */
+#pragma unroll
+    for (int i = 0; i < QPL; i++) toff[i] = 16 * tab_chunk(4 * j + i);
     f2_t qr[G][QPL], qi[G][QPL], qx[G][QPL];
     int cur_l = -1;
+    int l = 0, t = 0;                                    /* layer and tile of item k (no divisions) */
+    if (n_mine > 0) { l = it0 / a.tiles_per_layer; t = it0 - l * a.tiles_per_layer; }
+    int st = 0;
+    uint32_t phase = 0;
 
     for (int k = 0; k < n_mine; k++) {
-        const int st = k % S;
-        int l, c0;
-        const int cells = item_of(k, l, c0);
-        if (!mbar_wait(&full[st], (uint32_t)((k / S) & 1))) {
+        const int c0 = t * SC_T;
+        const int cells = max(0, min(SC_T, a.layer_rows[l] - c0));
+        if (!mbar_wait(&full[st], phase)) {
             if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
             s_abort = 1;
         }
         if (s_abort) break;
         const uint8_t *sb = stages + st * stage_bytes;
-        const float4 *tab = reinterpret_cast<const float4 *>(sb + plan.k_bytes());
-        const int32_t *slot = reinterpret_cast<const int32_t *>(sb + plan.k_bytes() + plan.tab_bytes(FC));
+        const uint8_t *tab = sb + plan.k_bytes();
+        const int32_t *slot = reinterpret_cast<const int32_t *>(tab + plan.tab_bytes(FC));
         const int cbeg = sub * cpw;
         const int u = l * KV + h;
         const int cend = active ? min(min(cells, a.n_rows[u] - c0), cbeg + cpw) : 0;
@@ -542,7 +580,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                 for (int g = 0; g < G; g++)
 #pragma unroll
                     for (int i = 0; i < QPL; i++) {
-                        const int q = j + 8 * ((i + cs4) & 3);     /* rotated: the pass's 4 cells hit 4 windows */
+                        const int q = 4 * j + i;
                         const float2 r = *reinterpret_cast<const float2 *>(src + g * 3 * FC + 2 * q);
                         const float2 m = *reinterpret_cast<const float2 *>(src + g * 3 * FC + FC + 2 * q);
                         qr[g][i] = pk(r.x * inv17, r.y * inv17);
@@ -551,77 +589,89 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                     }
             }
             const int hoff = h * a.row_bytes;
-            for (int cb = cbeg; cb < cend; cb += 4) {
-                const int c = cb + cs4;
-                const bool valid = c < cend;
-                float v[G];
+            for (int cb = cbeg; cb < cend; cb += 4 * WS_CPL) {
+                f2_t acc[WS_CPL][G];
+                int ts[WS_CPL];
 #pragma unroll
-                for (int g = 0; g < G; g++) v[g] = 0.f;
-                const int ts = valid ? slot[a.pos_shared ? c : h * SC_T + c] : -1;
-                if (ts >= 0) {
-                    const float4 *T = tab + ts * NQ;
-                    const uint8_t *row = sb + c * a.cell_stride + hoff;
-                    f2_t acc[G];
-#pragma unroll
-                    for (int g = 0; g < G; g++) acc[g] = 0ull;
+                for (int e = 0; e < WS_CPL; e++) {
+                    const int c = cb + 4 * e + cs4;
+                    const bool valid = c < cend;
+                    ts[e] = valid ? slot[a.pos_shared ? c : h * SC_T + c] : -1;
+                    const uint8_t *row = sb + (valid ? c : cbeg) * a.cell_stride + hoff;
+                    const uint8_t *trow = tab + max(ts[e], 0) * (FC * 8);
+                    uint4 kr4, ki4;                            /* f16: this lane's 8 real / 8 imag halves */
+                    if constexpr (KT == KT_F16) {
+                        kr4 = *reinterpret_cast<const uint4 *>(row + 16 * j);
+                        ki4 = *reinterpret_cast<const uint4 *>(row + 2 * FC + 16 * j);
+                    }
 #pragma unroll
                     for (int i = 0; i < QPL; i++) {
-                        const int q = j + 8 * ((i + cs4) & 3);
-                        const ulonglong2 cs = *reinterpret_cast<const ulonglong2 *>(T + q);   /* (C, S) pairs */
+                        const ulonglong2 cs = *reinterpret_cast<const ulonglong2 *>(trow + toff[i]);  /* (C, S) */
                         f2_t kr, ki;
-                        row_pair<KT, FC>(row, q, kr, ki);
+                        if constexpr (KT == KT_F16) {
+                            const uint32_t wr = i == 0 ? kr4.x : i == 1 ? kr4.y : i == 2 ? kr4.z : kr4.w;
+                            const uint32_t wi = i == 0 ? ki4.x : i == 1 ? ki4.y : i == 2 ? ki4.z : ki4.w;
+                            kr = h2_to_f2(wr);
+                            ki = h2_to_f2(wi);
+                        } else {
+                            row_pair<KT, FC>(row, 4 * j + i, kr, ki);
+                        }
                         const f2_t X = fma2(cs.x, kr, mul2(cs.y, ki));
-                        const f2_t Y = fma2(cs.x, ki, mul2(cs.y, neg2(kr)));
+                        const f2_t Y = sub2(mul2(cs.x, ki), mul2(cs.y, kr));
                         const f2_t m2 = fma2(kr, kr, mul2(ki, ki));
                         float m0, m1;
                         upk(m2, m0, m1);
                         const f2_t ka = pk(sqrt_approx(m0), sqrt_approx(m1));
 #pragma unroll
                         for (int g = 0; g < G; g++) {
-                            acc[g] = fma2(qr[g][i], X, acc[g]);
-                            acc[g] = fma2(qi[g][i], Y, acc[g]);
-                            acc[g] = fma2(qx[g][i], ka, acc[g]);
+                            acc[e][g] = i == 0 ? mul2(qr[g][i], X) : fma2(qr[g][i], X, acc[e][g]);
+                            acc[e][g] = fma2(qi[g][i], Y, acc[e][g]);
+                            acc[e][g] = fma2(qx[g][i], ka, acc[e][g]);
                         }
                     }
+                }
+#pragma unroll
+                for (int e = 0; e < WS_CPL; e++) {
+                    const int c = cb + 4 * e + cs4;
+                    const bool valid = c < cend;
+                    float v[G];
 #pragma unroll
                     for (int g = 0; g < G; g++) {
                         float a0, a1;
-                        upk(acc[g], a0, a1);
+                        upk(acc[e][g], a0, a1);
                         v[g] = a0 + a1;
                     }
-                }
-                /* reduce over the cell's 8 lanes: groups of 4 query heads transposed */
+                    float *out = a.raw + (int64_t)u * G * a.raw_stride + c0 + c;
+                    /* reduce over the cell's 8 lanes: groups of 4 query heads transposed;
+                     * a row outside the table scores 0 (and the status says so) */
 #pragma unroll
-                for (int g0 = 0; g0 + 4 <= G; g0 += 4) {
-                    const bool b1 = (j >> 2) & 1, b0 = (j >> 1) & 1;
-                    float x0 = b1 ? v[g0 + 2] : v[g0], x1 = b1 ? v[g0 + 3] : v[g0 + 1];
-                    const float y0 = b1 ? v[g0] : v[g0 + 2], y1 = b1 ? v[g0 + 1] : v[g0 + 3];
-                    x0 += __shfl_xor_sync(0xffffffffu, y0, 4);
-                    x1 += __shfl_xor_sync(0xffffffffu, y1, 4);
-                    float kk = b0 ? x1 : x0;
-                    const float oo = b0 ? x0 : x1;
-                    kk += __shfl_xor_sync(0xffffffffu, oo, 2);
-                    kk += __shfl_xor_sync(0xffffffffu, kk, 1);
-                    if (valid && (j & 1) == 0) ob[(g0 + 2 * b1 + b0) * SC_T + c] = kk;
-                }
+                    for (int g0 = 0; g0 + 4 <= G; g0 += 4) {
+                        const bool b1 = (j >> 2) & 1, b0 = (j >> 1) & 1;
+                        float x0 = b1 ? v[g0 + 2] : v[g0], x1 = b1 ? v[g0 + 3] : v[g0 + 1];
+                        const float y0 = b1 ? v[g0] : v[g0 + 2], y1 = b1 ? v[g0 + 1] : v[g0 + 3];
+                        x0 += __shfl_xor_sync(0xffffffffu, y0, 4);
+                        x1 += __shfl_xor_sync(0xffffffffu, y1, 4);
+                        float kk = b0 ? x1 : x0;
+                        const float oo = b0 ? x0 : x1;
+                        kk += __shfl_xor_sync(0xffffffffu, oo, 2);
+                        kk += __shfl_xor_sync(0xffffffffu, kk, 1);
+                        if (valid && (j & 1) == 0) out[(int64_t)(g0 + 2 * b1 + b0) * a.raw_stride] = ts[e] >= 0 ? kk : 0.f;
+                    }
 #pragma unroll
-                for (int g = G - G % 4; g < G; g++) {
-                    float kk = v[g];
-                    kk += __shfl_xor_sync(0xffffffffu, kk, 4);
-                    kk += __shfl_xor_sync(0xffffffffu, kk, 2);
-                    kk += __shfl_xor_sync(0xffffffffu, kk, 1);
-                    if (valid && j == 0) ob[g * SC_T + c] = kk;
+                    for (int g = G - G % 4; g < G; g++) {
+                        float kk = v[g];
+                        kk += __shfl_xor_sync(0xffffffffu, kk, 4);
+                        kk += __shfl_xor_sync(0xffffffffu, kk, 2);
+                        kk += __shfl_xor_sync(0xffffffffu, kk, 1);
+                        if (valid && j == 0) out[(int64_t)g * a.raw_stride] = ts[e] >= 0 ? kk : 0.f;
+                    }
                 }
             }
-            __syncwarp();
-            /* cells [cbeg, cend): write out */
-            for (int i = lane; i < G * cpw; i += 32) {
-                const int g = i / cpw, c = cbeg + (i - g * cpw);
-                if (c < cend) a.raw[((int64_t)u * G + g) * a.raw_stride + c0 + c] = ob[g * SC_T + c];
-            }
-            __syncwarp();
         }
+        __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
+        if (++st == S) { st = 0; phase ^= 1u; }
+        if (++t == a.tiles_per_layer) { t = 0; l++; }
     }
 }
 
@@ -748,34 +798,37 @@ __device__ float walk_chain(const float *ring_base, uint64_t *bars, int n, int n
             const int M = (bits >> 31) ? -mabs : mabs;
             /* live elements of this lane: [p, cnt) within [16*lane, 16*lane+16) */
             const int lo = max(0, p - lane * ZW_EPL), hi = min(ZW_EPL, cnt - lane * ZW_EPL);
-            const unsigned live = hi > lo ? (((hi >= 32 ? 0u : (1u << hi)) - 1u) & ~((1u << lo) - 1u)) : 0u;
-            /* increments v/ulp rounded to the grid: q = v * 2^(23-E) is exact while
-             * |v| < 2^(E+1); ties keep the lower candidate and are settled below */
+            /* Increments: q = v * 2^(23-E) = v/ulp exactly.  For |q| < 2^22, f = q + 1.5*2^23
+             * lies in (2^23, 2^24) where the fp32 grid is the integers, so f rounds q to
+             * the nearest integer (ties to even) and bits(f) - bits(1.5*2^23) is that
+             * integer.  A tie (|q - r| == 1/2) takes the lower candidate and is settled
+             * by parity below.  |q| >= 2^22 (or not finite) marks the element "out":
+             * it is added with a plain fp32 add.  Dead elements count as 0. */
             const float scale = __int_as_float((150 - E) << 23);
-            const uint32_t lim = (uint32_t)(E + 128) << 23;          /* bits of 2^(E+1) */
             /* increments and their sums are kept modulo 2^32: every value that is used
              * (partials inside the binade) is < 2^24 in magnitude, so wrap-around of
              * discarded ones does no harm */
             uint32_t d[ZW_EPL];
-            unsigned tie = 0, bad = 0;
+            bool any_tie = false, any_out = false;
             uint32_t lsum = 0;
-            int pmin = INT_MAX, pmax = INT_MIN;         /* extremes of this lane's live prefix sums */
+            int pmin = 0x7fffffff, pmax = -0x7fffffff - 1;   /* extremes of this lane's prefix sums */
 #pragma unroll
             for (int t = 0; t < ZW_EPL; t++) {
-                const float q = v[t] * scale;
-                const float r = rintf(q);
-                const bool isb = (__float_as_uint(v[t]) & 0x7fffffffu) >= lim;
-                const bool ist = fabsf(q - r) == 0.5f;
-                uint32_t dd = (uint32_t)(ist ? (int)(q - 0.5f) : __float2int_rn(r));
-                const bool on = (live >> t) & 1;
-                dd = (on && !isb) ? dd : 0u;
-                tie |= (on && ist && !isb ? 1u : 0u) << t;
-                bad |= (on && isb ? 1u : 0u) << t;
+                const float x = (t >= lo && t < hi) ? v[t] : 0.f;
+                const float q = x * scale;
+                const bool out = !(fabsf(q) < 0x1p22f);
+                const float f = __fadd_rn(q, 0x1.8p23f);
+                const float fr = __fsub_rn(q, __fsub_rn(f, 0x1.8p23f));
+                const bool ist = fabsf(fr) == 0.5f;
+                uint32_t dd = (uint32_t)(__float_as_int(f) - 0x4b400000) - ((ist && fr < 0.f) ? 1u : 0u);
+                dd = out ? 0u : dd;
+                any_tie |= ist && !out;
+                any_out |= out;
                 d[t] = dd;
                 lsum += dd;
-                /* |increment| <= 2^24, so a lane's prefix sums fit an int */
-                pmin = on ? min(pmin, (int)lsum) : pmin;
-                pmax = on ? max(pmax, (int)lsum) : pmax;
+                /* |increment| <= 2^22, so a lane's prefix sums fit an int */
+                pmin = min(pmin, (int)lsum);
+                pmax = max(pmax, (int)lsum);
             }
             /* exclusive warp scan of the lane totals */
             uint32_t inc = lsum;
@@ -785,17 +838,17 @@ __device__ float walk_chain(const float *ring_base, uint64_t *bars, int n, int n
                 if (lane >= m) inc += y;
             }
             uint32_t off = inc - lsum;                       /* sum of increments of earlier lanes */
-            /* Whole step at once when no live element is a tie or out of the binade
-             * and both extremes of every lane's partial significands lie inside
-             * [2^23 + 1, 2^24 - 1] (then all of them do).  A lane whose earlier
-             * lanes all pass has an exact `off`; the first failing lane therefore
+            /* Whole step at once when no element is a tie or out and both extremes of
+             * every lane's partial significands (dead elements repeat the partial before
+             * them) lie inside [2^23 + 1, 2^24 - 1] -- then all of them do.  A lane whose
+             * earlier lanes all pass has an exact `off`; the first failing lane therefore
              * sees true values and fails, so wrap-around cannot pass a bad step. */
             {
                 const uint32_t sg = M > 0 ? 1u : 0xffffffffu;
                 const uint32_t b0 = (uint32_t)M + off;
                 const bool in_lo = ((b0 + (uint32_t)pmin) * sg - ((1u << 23) + 1u)) <= (1u << 23) - 2u;
                 const bool in_hi = ((b0 + (uint32_t)pmax) * sg - ((1u << 23) + 1u)) <= (1u << 23) - 2u;
-                const bool ok = tie == 0 && bad == 0 && (pmin > pmax || (in_lo && in_hi));
+                const bool ok = !any_tie && !any_out && in_lo && in_hi;
                 if (__all_sync(0xffffffffu, ok)) {
                     const uint32_t part = __shfl_sync(0xffffffffu, (uint32_t)M + inc, 31);
                     const uint32_t a = M > 0 ? part : 0u - part;
@@ -803,6 +856,18 @@ __device__ float walk_chain(const float *ring_base, uint64_t *bars, int n, int n
                     p = cnt;
                     continue;
                 }
+            }
+            /* slow step: per-element tie / out / live masks */
+            const unsigned live = hi > lo ? (((hi >= 32 ? 0u : (1u << hi)) - 1u) & ~((1u << lo) - 1u)) : 0u;
+            unsigned tie = 0, bad = 0;
+#pragma unroll
+            for (int t = 0; t < ZW_EPL; t++) {
+                const float x = (t >= lo && t < hi) ? v[t] : 0.f;
+                const float q = x * scale;
+                const bool out = !(fabsf(q) < 0x1p22f);
+                const float fr = __fsub_rn(q, __fsub_rn(__fadd_rn(q, 0x1.8p23f), 0x1.8p23f));
+                tie |= (!out && fabsf(fr) == 0.5f ? 1u : 0u) << t;
+                bad |= (out ? 1u : 0u) << t;
             }
             /* ties in element order: the candidate with an even significand */
             unsigned tmask = __ballot_sync(0xffffffffu, tie != 0);
