@@ -431,10 +431,12 @@ static WsPlan ws_plan(const tria_ctx *c, const tria_kv_view *v) {
     p.tab_rows = v->pos_shared ? SC_T : SC_T * v->n_head_kv;
     p.pos_ints = p.tab_rows;
     p.G = (int)c->G;
-    for (int s = 4; s >= 2; s--) {
-        p.stages = s;
-        if (p.total((int)c->fc) <= 220 * 1024) return p;
-    }
+    for (int ps = 2; ps >= 1; ps--)
+        for (int s = 4; s >= 2; s--) {
+            p.stages = s;
+            p.part_slots = ps;
+            if (p.total((int)c->fc) <= 220 * 1024) return p;
+        }
     p.stages = 0;
     return p;
 }

@@ -259,8 +259,9 @@ constexpr int WS_THREADS = (WS_CWARPS + 4) * 32;   /* + a producer warpgroup, on
  * most the launch total, or the increase would wait forever; the host checks
  * the compiled register count before every launch. */
 constexpr int WS_LAUNCH_REGS = 168;
-constexpr int WS_PRODUCER_REGS = 56;
-constexpr int WS_CONSUMER_REGS = 224;
+constexpr int WS_PRODUCER_REGS = 72;
+constexpr int WS_CONSUMER_REGS = 216;
+constexpr int WS_RWARPS = 3;           /* reducer warps: the producer warpgroup's other three */
 static_assert(4 * 32 * WS_PRODUCER_REGS + WS_CWARPS * 32 * WS_CONSUMER_REGS <= WS_THREADS * WS_LAUNCH_REGS,
               "register split exceeds the launch allocation");
 static_assert(WS_THREADS * WS_LAUNCH_REGS <= 65536, "launch allocation exceeds the register file");
@@ -284,15 +285,20 @@ struct TmaScoreArgs {
     int32_t n_rows[TRIA_MAX_UNITS];
 };
 
-/* Shared-memory plan of k_score_ws, shared by host and device. */
+/* Shared-memory plan of k_score_ws, shared by host and device.  Per work item
+ * the consumers leave, for each of its rows, 8 lanes x GP partial sums
+ * (GP = G padded to 4 or 8) in one of part_slots partial buffers. */
 struct WsPlan {
-    int stages, cell_bytes, tab_rows, pos_ints, G;
+    int stages, cell_bytes, tab_rows, pos_ints, G, part_slots;
+    __host__ __device__ int gp() const { return G <= 4 ? 4 : 8; }
     __host__ __device__ int k_bytes() const { return SC_T * cell_bytes; }
     __host__ __device__ int tab_bytes(int fc) const { return tab_rows * fc * 8; }
     __host__ __device__ int stage_bytes(int fc) const { return k_bytes() + tab_bytes(fc) + pos_ints * 4; }
     __host__ __device__ int ring_bytes() const { return WS_POS_RING * pos_ints * 4; }
+    __host__ __device__ int part_floats() const { return WS_CWARPS * SC_T * 8 * gp(); }   /* one buffer */
     __host__ __device__ int total(int fc) const {
-        return stages * stage_bytes(fc) + ring_bytes() + (2 * stages + WS_POS_RING) * 8;
+        return stages * stage_bytes(fc) + ring_bytes() + part_slots * part_floats() * 4 +
+               (2 * stages + WS_POS_RING + 2 * part_slots) * 8;
     }
 };
 
@@ -335,7 +341,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
 }
 
 typedef unsigned long long f2_t;          /* two packed fp32 for the f32x2 instructions */
-__device__ __forceinline__ f2_t pk(float a, float b) {
+__device__ __forceinline__ f2_t pk2(float a, float b) {
     f2_t r;
     asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
     return r;
@@ -379,8 +385,8 @@ __device__ __forceinline__ void row_pair(const uint8_t *row, int q, f2_t &kr, f2
         const float sm = __half2float(*reinterpret_cast<const __half *>(bm));
         const char2 vr = *reinterpret_cast<const char2 *>(br + 2 + (dr & 31));
         const char2 vm = *reinterpret_cast<const char2 *>(bm + 2 + (dm & 31));
-        kr = pk((float)vr.x * sr, (float)vr.y * sr);
-        ki = pk((float)vm.x * sm, (float)vm.y * sm);
+        kr = pk2((float)vr.x * sr, (float)vr.y * sr);
+        ki = pk2((float)vm.x * sm, (float)vm.y * sm);
     }
 }
 
@@ -404,11 +410,14 @@ __device__ __forceinline__ void row_pair(const uint8_t *row, int q, f2_t &kr, f2
  * contiguous bytes of K per instruction and, through the chunk rotation of
  * tab_chunk(), eight distinct bank groups of its table row.  The lane's
  * q-centre terms (pre-scaled by 1/17) and norm terms stay in registers for
- * the whole layer; the math runs as packed f32x2 FMAs; the G sums are
- * reduced across the 8 lanes with a transposing butterfly and written
- * straight to the raw-score rows.  The producer warpgroup hands its
- * registers to the consumers (setmaxnreg).  Every wait is bounded
- * (ST_TIMEOUT).
+ * the whole layer; the math runs as packed f32x2 FMAs.  Each lane leaves
+ * its G partial sums per cell in a partial buffer (8 lanes x GP floats per
+ * row) and moves on; the producer warpgroup's other three warps sum each
+ * row's 8 partials and write the raw scores, so no consumer waits on a
+ * shuffle reduction.  The producer warpgroup runs on WS_PRODUCER_REGS
+ * registers and hands the rest to the consumers (setmaxnreg); each role's
+ * code sits after its own setmaxnreg so the compiler budgets it alone.
+ * Every wait is bounded (ST_TIMEOUT).
  */
 template <int KT, int G>
 __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a, const WsPlan plan) {
@@ -419,15 +428,20 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
     const int stage_bytes = plan.stage_bytes(FC);
     uint8_t *stages = smem;
     int32_t *ring = reinterpret_cast<int32_t *>(smem + S * stage_bytes);              /* [WS_POS_RING][pos_ints] */
-    uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(ring) + plan.ring_bytes());
+    float *part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ring) + plan.ring_bytes());
+    uint64_t *full = reinterpret_cast<uint64_t *>(part + plan.part_slots * plan.part_floats());
     uint64_t *empty = full + S;
     uint64_t *posbar = empty + S;
+    uint64_t *pfull = posbar + WS_POS_RING;              /* partials of an item written */
+    uint64_t *pfree = pfull + plan.part_slots;           /* partials of an item reduced */
+    const int P = plan.part_slots, GP = plan.gp();
     __shared__ volatile int s_abort;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
         for (int i = 0; i < S; i++) { mbar_init(&full[i], 1); mbar_init(&empty[i], WS_CWARPS); }
         for (int i = 0; i < WS_POS_RING; i++) mbar_init(&posbar[i], 1);
+        for (int i = 0; i < P; i++) { mbar_init(&pfull[i], WS_CWARPS); mbar_init(&pfree[i], WS_RWARPS); }
         s_abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -443,12 +457,134 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         return max(0, min(SC_T, a.layer_rows[l] - c0));
     };
 
-    if (warp >= WS_CWARPS) {
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(WS_PRODUCER_REGS));
-        if (warp != WS_CWARPS) return;
-    } else {
+    /* Register split: each role's code sits after its own setmaxnreg. */
+    if (warp < WS_CWARPS) {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(WS_CONSUMER_REGS));
+        /* ---------------- consumers ---------------- */
+        const int j = lane & 7, cs4 = lane >> 3;             /* chunk group (pairs 8j..8j+7), cell of the pass */
+        const int wph = max(1, WS_CWARPS / KV);              /* warps per head */
+        const bool active = warp < KV * wph;
+        const int h = active ? warp % KV : 0, sub = warp / KV;
+        const int cpw = (SC_T + wph - 1) / wph;              /* cells of a tile per warp (<= 4 * WS_CPL) */
+        const float inv17 = 1.0f / 17.0f;
+        int toff[QPL];                                       /* bytes of chunk 4j+i within a table row */
+    #pragma unroll
+        for (int i = 0; i < QPL; i++) toff[i] = 16 * tab_chunk(4 * j + i);
+        f2_t qr[G][QPL], qi[G][QPL], qx[G][QPL];
+        int cur_l = -1;
+        int l = 0, t = 0;                                    /* layer and tile of item k (no divisions) */
+        if (n_mine > 0) { l = it0 / a.tiles_per_layer; t = it0 - l * a.tiles_per_layer; }
+        int st = 0, pk = 0;
+        uint32_t phase = 0, pph = 0;
+
+        for (int k = 0; k < n_mine; k++) {
+            const int c0 = t * SC_T;
+            const int cells = max(0, min(SC_T, a.layer_rows[l] - c0));
+            if (!mbar_wait(&full[st], phase)) {
+                if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
+                s_abort = 1;
+            }
+            if (s_abort) break;
+            const uint8_t *sb = stages + st * stage_bytes;
+            const uint8_t *tab = sb + plan.k_bytes();
+            const int32_t *slot = reinterpret_cast<const int32_t *>(tab + plan.tab_bytes(FC));
+            const int cb = sub * cpw;
+            const int u = l * KV + h;
+            const int cend = active ? min(min(cells, a.n_rows[u] - c0), cb + cpw) : 0;
+            f2_t acc[WS_CPL][G];
+            int ts[WS_CPL];
+            if (cb < cend) {
+                if (l != cur_l) {                                  /* this lane's q terms for layer l */
+                    cur_l = l;
+                    const int ml = a.layer0 + l, mh = a.head0 + h;
+                    const float *src = a.q + ((size_t)(ml * a.H + mh * G) * 3) * FC;
+    #pragma unroll
+                    for (int g = 0; g < G; g++)
+    #pragma unroll
+                        for (int i = 0; i < QPL; i++) {
+                            const int q = 4 * j + i;
+                            const float2 r = *reinterpret_cast<const float2 *>(src + g * 3 * FC + 2 * q);
+                            const float2 m = *reinterpret_cast<const float2 *>(src + g * 3 * FC + FC + 2 * q);
+                            qr[g][i] = pk2(r.x * inv17, r.y * inv17);
+                            qi[g][i] = pk2(m.x * inv17, m.y * inv17);
+                            qx[g][i] = *reinterpret_cast<const f2_t *>(src + g * 3 * FC + 2 * FC + 2 * q);
+                        }
+                }
+                const int hoff = h * a.row_bytes;
+    #pragma unroll
+                for (int e = 0; e < WS_CPL; e++) {
+                    const int c = cb + 4 * e + cs4;
+                    const bool valid = c < cend;
+                    ts[e] = valid ? slot[a.pos_shared ? c : h * SC_T + c] : -1;
+                    const uint8_t *row = sb + (valid ? c : cb) * a.cell_stride + hoff;
+                    const uint8_t *trow = tab + max(ts[e], 0) * (FC * 8);
+                    uint4 kr4, ki4;                                /* f16: this lane's 8 real / 8 imag halves */
+                    if constexpr (KT == KT_F16) {
+                        kr4 = *reinterpret_cast<const uint4 *>(row + 16 * j);
+                        ki4 = *reinterpret_cast<const uint4 *>(row + 2 * FC + 16 * j);
+                    }
+    #pragma unroll
+                    for (int i = 0; i < QPL; i++) {
+                        const ulonglong2 cs = *reinterpret_cast<const ulonglong2 *>(trow + toff[i]);  /* (C, S) */
+                        f2_t kr, ki;
+                        if constexpr (KT == KT_F16) {
+                            kr = h2_to_f2(i == 0 ? kr4.x : i == 1 ? kr4.y : i == 2 ? kr4.z : kr4.w);
+                            ki = h2_to_f2(i == 0 ? ki4.x : i == 1 ? ki4.y : i == 2 ? ki4.z : ki4.w);
+                        } else {
+                            row_pair<KT, FC>(row, 4 * j + i, kr, ki);
+                        }
+                        const f2_t X = fma2(cs.x, kr, mul2(cs.y, ki));
+                        const f2_t Y = sub2(mul2(cs.x, ki), mul2(cs.y, kr));
+                        const f2_t m2 = fma2(kr, kr, mul2(ki, ki));
+                        float m0, m1;
+                        upk(m2, m0, m1);
+                        const f2_t ka = pk2(sqrt_approx(m0), sqrt_approx(m1));
+    #pragma unroll
+                        for (int g = 0; g < G; g++) {
+                            acc[e][g] = i == 0 ? mul2(qr[g][i], X) : fma2(qr[g][i], X, acc[e][g]);
+                            acc[e][g] = fma2(qi[g][i], Y, acc[e][g]);
+                            acc[e][g] = fma2(qx[g][i], ka, acc[e][g]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);           /* the stage is no longer read */
+            /* partial sums -> buffer pk once the reducers are done with its previous item */
+            if (!mbar_wait(&pfree[pk], pph ^ 1u)) {
+                if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
+                s_abort = 1;
+            }
+            if (s_abort) break;
+            if (cb < cend) {
+                float *pb = part + pk * plan.part_floats();
+    #pragma unroll
+                for (int e = 0; e < WS_CPL; e++) {
+                    const int c = cb + 4 * e + cs4;
+                    if (c < cend) {
+                        /* a row outside the table scores 0 (the status says so) */
+                        float v[8];
+    #pragma unroll
+                        for (int g = 0; g < 8; g++) {
+                            float a0 = 0.f, a1 = 0.f;
+                            if (g < G) upk(acc[e][g], a0, a1);
+                            v[g] = ts[e] >= 0 ? a0 + a1 : 0.f;
+                        }
+                        float4 *dst = reinterpret_cast<float4 *>(pb + ((h * SC_T + c) * 8 + j) * GP);
+                        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+                        if (G > 4) dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pfull[pk]);
+            if (++st == S) { st = 0; phase ^= 1u; }
+            if (++pk == P) { pk = 0; pph ^= 1u; }
+            if (++t == a.tiles_per_layer) { t = 0; l++; }
+        }
+        return;
     }
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(WS_PRODUCER_REGS));
 
     if (warp == WS_CWARPS) {
         /* ---------------- producer ---------------- */
@@ -540,139 +676,56 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         return;
     }
 
-    /* ---------------- consumers ---------------- */
-    const int j = lane & 7, cs4 = lane >> 3;             /* chunk group (pairs 8j..8j+7), cell of the pass */
-    const int wph = max(1, WS_CWARPS / KV);              /* warps per head */
-    const bool active = warp < KV * wph;
-    const int h = active ? warp % KV : 0, sub = warp / KV;
-    const int cpw = (SC_T + wph - 1) / wph;              /* cells of a tile per warp */
-    const float inv17 = 1.0f / 17.0f;
-    int toff[QPL];                                       /* bytes of chunk 4j+i within a table row */
-#pragma unroll
-    for (int i = 0; i < QPL; i++) toff[i] = 16 * tab_chunk(4 * j + i);
-    f2_t qr[G][QPL], qi[G][QPL], qx[G][QPL];
-    int cur_l = -1;
-    int l = 0, t = 0;                                    /* layer and tile of item k (no divisions) */
-    if (n_mine > 0) { l = it0 / a.tiles_per_layer; t = it0 - l * a.tiles_per_layer; }
-    int st = 0;
-    uint32_t phase = 0;
-
-    for (int k = 0; k < n_mine; k++) {
-        const int c0 = t * SC_T;
-        const int cells = max(0, min(SC_T, a.layer_rows[l] - c0));
-        if (!mbar_wait(&full[st], phase)) {
-            if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
-            s_abort = 1;
-        }
-        if (s_abort) break;
-        const uint8_t *sb = stages + st * stage_bytes;
-        const uint8_t *tab = sb + plan.k_bytes();
-        const int32_t *slot = reinterpret_cast<const int32_t *>(tab + plan.tab_bytes(FC));
-        const int cbeg = sub * cpw;
-        const int u = l * KV + h;
-        const int cend = active ? min(min(cells, a.n_rows[u] - c0), cbeg + cpw) : 0;
-        if (cbeg < cend) {
-            if (l != cur_l) {                                  /* this lane's q terms for layer l */
-                cur_l = l;
-                const int ml = a.layer0 + l, mh = a.head0 + h;
-                const float *src = a.q + ((size_t)(ml * a.H + mh * G) * 3) * FC;
-#pragma unroll
-                for (int g = 0; g < G; g++)
-#pragma unroll
-                    for (int i = 0; i < QPL; i++) {
-                        const int q = 4 * j + i;
-                        const float2 r = *reinterpret_cast<const float2 *>(src + g * 3 * FC + 2 * q);
-                        const float2 m = *reinterpret_cast<const float2 *>(src + g * 3 * FC + FC + 2 * q);
-                        qr[g][i] = pk(r.x * inv17, r.y * inv17);
-                        qi[g][i] = pk(m.x * inv17, m.y * inv17);
-                        qx[g][i] = *reinterpret_cast<const f2_t *>(src + g * 3 * FC + 2 * FC + 2 * q);
-                    }
+    {
+        /* ---------------- reducers ---------------- */
+        /* Row r = h * SC_T + c of an item: sum its 8 lanes' partials per query
+         * head and write the raw scores (consecutive lanes: consecutive cells). */
+        const int rw = warp - WS_CWARPS - 1;
+        int l = 0, t = 0;
+        if (n_mine > 0) { l = it0 / a.tiles_per_layer; t = it0 - l * a.tiles_per_layer; }
+        int pk = 0;
+        uint32_t pph = 0;
+        for (int k = 0; k < n_mine; k++) {
+            if (!mbar_wait(&pfull[pk], pph)) {
+                if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
+                s_abort = 1;
             }
-            const int hoff = h * a.row_bytes;
-            for (int cb = cbeg; cb < cend; cb += 4 * WS_CPL) {
-                f2_t acc[WS_CPL][G];
-                int ts[WS_CPL];
+            if (s_abort) break;
+            const int c0 = t * SC_T;
+            const int cells = max(0, min(SC_T, a.layer_rows[l] - c0));
+            const float *pb = part + pk * plan.part_floats();
+            for (int r = rw * 32 + lane; r < KV * SC_T; r += WS_RWARPS * 32) {
+                const int h = r / SC_T, c = r - h * SC_T;
+                const int u = l * KV + h;
+                if (c >= min(cells, a.n_rows[u] - c0)) continue;
+                const float *row = pb + r * 8 * GP;
+                float sum[8];
 #pragma unroll
-                for (int e = 0; e < WS_CPL; e++) {
-                    const int c = cb + 4 * e + cs4;
-                    const bool valid = c < cend;
-                    ts[e] = valid ? slot[a.pos_shared ? c : h * SC_T + c] : -1;
-                    const uint8_t *row = sb + (valid ? c : cbeg) * a.cell_stride + hoff;
-                    const uint8_t *trow = tab + max(ts[e], 0) * (FC * 8);
-                    uint4 kr4, ki4;                            /* f16: this lane's 8 real / 8 imag halves */
-                    if constexpr (KT == KT_F16) {
-                        kr4 = *reinterpret_cast<const uint4 *>(row + 16 * j);
-                        ki4 = *reinterpret_cast<const uint4 *>(row + 2 * FC + 16 * j);
-                    }
+                for (int g = 0; g < 8; g++) sum[g] = 0.f;
 #pragma unroll
-                    for (int i = 0; i < QPL; i++) {
-                        const ulonglong2 cs = *reinterpret_cast<const ulonglong2 *>(trow + toff[i]);  /* (C, S) */
-                        f2_t kr, ki;
-                        if constexpr (KT == KT_F16) {
-                            const uint32_t wr = i == 0 ? kr4.x : i == 1 ? kr4.y : i == 2 ? kr4.z : kr4.w;
-                            const uint32_t wi = i == 0 ? ki4.x : i == 1 ? ki4.y : i == 2 ? ki4.z : ki4.w;
-                            kr = h2_to_f2(wr);
-                            ki = h2_to_f2(wi);
-                        } else {
-                            row_pair<KT, FC>(row, 4 * j + i, kr, ki);
-                        }
-                        const f2_t X = fma2(cs.x, kr, mul2(cs.y, ki));
-                        const f2_t Y = sub2(mul2(cs.x, ki), mul2(cs.y, kr));
-                        const f2_t m2 = fma2(kr, kr, mul2(ki, ki));
-                        float m0, m1;
-                        upk(m2, m0, m1);
-                        const f2_t ka = pk(sqrt_approx(m0), sqrt_approx(m1));
+                for (int i = 0; i < 8; i++) {
+                    const int jj = (i + lane) & 7;               /* rotated: a phase's 8 rows hit 8 bank groups */
 #pragma unroll
-                        for (int g = 0; g < G; g++) {
-                            acc[e][g] = i == 0 ? mul2(qr[g][i], X) : fma2(qr[g][i], X, acc[e][g]);
-                            acc[e][g] = fma2(qi[g][i], Y, acc[e][g]);
-                            acc[e][g] = fma2(qx[g][i], ka, acc[e][g]);
+                    for (int g4 = 0; g4 < 8; g4 += 4) {
+                        if (g4 < GP) {
+                            const float4 w = *reinterpret_cast<const float4 *>(row + jj * GP + g4);
+                            sum[g4] += w.x; sum[g4 + 1] += w.y; sum[g4 + 2] += w.z; sum[g4 + 3] += w.w;
                         }
                     }
                 }
+                float *out = a.raw + (int64_t)u * G * a.raw_stride + c0 + c;
 #pragma unroll
-                for (int e = 0; e < WS_CPL; e++) {
-                    const int c = cb + 4 * e + cs4;
-                    const bool valid = c < cend;
-                    float v[G];
-#pragma unroll
-                    for (int g = 0; g < G; g++) {
-                        float a0, a1;
-                        upk(acc[e][g], a0, a1);
-                        v[g] = a0 + a1;
-                    }
-                    float *out = a.raw + (int64_t)u * G * a.raw_stride + c0 + c;
-                    /* reduce over the cell's 8 lanes: groups of 4 query heads transposed;
-                     * a row outside the table scores 0 (and the status says so) */
-#pragma unroll
-                    for (int g0 = 0; g0 + 4 <= G; g0 += 4) {
-                        const bool b1 = (j >> 2) & 1, b0 = (j >> 1) & 1;
-                        float x0 = b1 ? v[g0 + 2] : v[g0], x1 = b1 ? v[g0 + 3] : v[g0 + 1];
-                        const float y0 = b1 ? v[g0] : v[g0 + 2], y1 = b1 ? v[g0 + 1] : v[g0 + 3];
-                        x0 += __shfl_xor_sync(0xffffffffu, y0, 4);
-                        x1 += __shfl_xor_sync(0xffffffffu, y1, 4);
-                        float kk = b0 ? x1 : x0;
-                        const float oo = b0 ? x0 : x1;
-                        kk += __shfl_xor_sync(0xffffffffu, oo, 2);
-                        kk += __shfl_xor_sync(0xffffffffu, kk, 1);
-                        if (valid && (j & 1) == 0) out[(int64_t)(g0 + 2 * b1 + b0) * a.raw_stride] = ts[e] >= 0 ? kk : 0.f;
-                    }
-#pragma unroll
-                    for (int g = G - G % 4; g < G; g++) {
-                        float kk = v[g];
-                        kk += __shfl_xor_sync(0xffffffffu, kk, 4);
-                        kk += __shfl_xor_sync(0xffffffffu, kk, 2);
-                        kk += __shfl_xor_sync(0xffffffffu, kk, 1);
-                        if (valid && j == 0) out[(int64_t)g * a.raw_stride] = ts[e] >= 0 ? kk : 0.f;
-                    }
-                }
+                for (int g = 0; g < G; g++) out[(int64_t)g * a.raw_stride] = sum[g];
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pfree[pk]);
+            if (++pk == P) { pk = 0; pph ^= 1u; }
+            if (++t == a.tiles_per_layer) { t = 0; l++; }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
-        if (++st == S) { st = 0; phase ^= 1u; }
-        if (++t == a.tiles_per_layer) { t = 0; l++; }
+        return;
     }
+
+
 }
 
 /* ------------------------------------------------------------------ */
