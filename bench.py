@@ -74,9 +74,21 @@ def step_bytes(c, units, keep):
     return units * (n * rb + 4 * keep * rb + 4 * n + 8 * keep)
 
 
-def score_kernel_bytes(c, units):
+def score_kernel_bytes(c, units, layers):
+    """Algorithmic DRAM bytes of one scoring launch over `units` (layer, kv-head)
+    units of n rows: every K row once, the shared position row once per layer,
+    the delta table rows once (n rows of fc*8 bytes), and the G raw scores of
+    every row written."""
     rb = workloads.row_bytes(c["type"], c["hd"])
-    return units * c["n"] * (rb + 4)
+    n, G, fc = c["n"], c["H"] // c["KV"], c["hd"] // 2
+    return units * n * rb + layers * n * 4 + n * fc * 8 + units * G * n * 4
+
+
+def score_kernel_flops(c, units):
+    """fp32 FLOPs of the scoring math per launch: per row and frequency pair
+    X, Y and |k|^2 (9 flops), then 3 FMAs (6 flops) per query head."""
+    G, fc = c["H"] // c["KV"], c["hd"] // 2
+    return units * c["n"] * fc * (9 + 6 * G)
 
 
 def measured_peak():
@@ -396,11 +408,12 @@ def run_ours(args):
     total_units = units * world
     value = total_units * n / (ms_max / 1e3)
     peak, peak_src = measured_peak()
-    sb = score_kernel_bytes(c, units)
+    sb = score_kernel_bytes(c, units, L)
     score_ms = stage.get("score")
     achieved = sb / (score_ms / 1e3) / 1e9 if score_ms else None
     wl = args.config
-    traffic = ncu_traffic("k_score_raw", wl)
+    traffic = ncu_traffic("k_score_ws", wl)
+    flops = score_kernel_flops(c, units)
     step_b = step_bytes(c, units, keep)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -412,10 +425,12 @@ def run_ours(args):
                    "heads": c["H"], "head_dim": c["hd"], "rows": n, "kept": keep,
                    "shard": f"{n_head_kv} kv heads x {L} layers per rank",
                    "l2": "inputs larger than L2 (no flush)"},
-        "roofline": {"bound": "hbm", "kernel": "k_score_raw", "achieved": achieved, "peak": peak,
+        "roofline": {"bound": "hbm", "kernel": "k_score_ws", "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
                      "traffic": traffic, "peak_source": f"{peak_src} hbm_gbs",
-                     "algorithmic_bytes_per_launch": sb, "launch_ms": score_ms},
+                     "algorithmic_bytes_per_launch": sb, "launch_ms": score_ms,
+                     "fp32_flops_per_launch": flops,
+                     "fp32_tflops": flops / (score_ms / 1e3) / 1e12 if score_ms else None},
         "step_roofline": {"bytes_per_step": step_b, "achieved": step_b / (ms / 1e3) / 1e9,
                           "frac": step_b / (ms / 1e3) / 1e9 / peak, "unit": "GB/s"},
         "stage_ms": stage,

@@ -468,7 +468,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         const int cpw = (SC_T + wph - 1) / wph;              /* cells of a tile per warp (<= 4 * WS_CPL) */
         const float inv17 = 1.0f / 17.0f;
         int toff[QPL];                                       /* bytes of chunk 4j+i within a table row */
-    #pragma unroll
+#pragma unroll
         for (int i = 0; i < QPL; i++) toff[i] = 16 * tab_chunk(4 * j + i);
         f2_t qr[G][QPL], qi[G][QPL], qx[G][QPL];
         int cur_l = -1;
@@ -498,9 +498,9 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                     cur_l = l;
                     const int ml = a.layer0 + l, mh = a.head0 + h;
                     const float *src = a.q + ((size_t)(ml * a.H + mh * G) * 3) * FC;
-    #pragma unroll
+#pragma unroll
                     for (int g = 0; g < G; g++)
-    #pragma unroll
+#pragma unroll
                         for (int i = 0; i < QPL; i++) {
                             const int q = 4 * j + i;
                             const float2 r = *reinterpret_cast<const float2 *>(src + g * 3 * FC + 2 * q);
@@ -511,7 +511,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                         }
                 }
                 const int hoff = h * a.row_bytes;
-    #pragma unroll
+#pragma unroll
                 for (int e = 0; e < WS_CPL; e++) {
                     const int c = cb + 4 * e + cs4;
                     const bool valid = c < cend;
@@ -523,7 +523,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                         kr4 = *reinterpret_cast<const uint4 *>(row + 16 * j);
                         ki4 = *reinterpret_cast<const uint4 *>(row + 2 * FC + 16 * j);
                     }
-    #pragma unroll
+#pragma unroll
                     for (int i = 0; i < QPL; i++) {
                         const ulonglong2 cs = *reinterpret_cast<const ulonglong2 *>(trow + toff[i]);  /* (C, S) */
                         f2_t kr, ki;
@@ -539,7 +539,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                         float m0, m1;
                         upk(m2, m0, m1);
                         const f2_t ka = pk2(sqrt_approx(m0), sqrt_approx(m1));
-    #pragma unroll
+#pragma unroll
                         for (int g = 0; g < G; g++) {
                             acc[e][g] = i == 0 ? mul2(qr[g][i], X) : fma2(qr[g][i], X, acc[e][g]);
                             acc[e][g] = fma2(qi[g][i], Y, acc[e][g]);
@@ -558,13 +558,13 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
             if (s_abort) break;
             if (cb < cend) {
                 float *pb = part + pk * plan.part_floats();
-    #pragma unroll
+#pragma unroll
                 for (int e = 0; e < WS_CPL; e++) {
                     const int c = cb + 4 * e + cs4;
                     if (c < cend) {
                         /* a row outside the table scores 0 (the status says so) */
                         float v[8];
-    #pragma unroll
+#pragma unroll
                         for (int g = 0; g < 8; g++) {
                             float a0 = 0.f, a1 = 0.f;
                             if (g < G) upk(acc[e][g], a0, a1);
