@@ -423,27 +423,31 @@ static WsPlan ws_plan(const tria_ctx *c, const tria_kv_view *v) {
     WsPlan p{};
     const int64_t rb = view_row_bytes(v->type, (int)c->hd);
     if (v->head_stride != rb || v->cell_stride != rb * v->n_head_kv) return p;
-    if (v->cell_stride % 16 || v->n_head_kv > WS_CWARPS || v->cell_stride * SC_T > (1 << 20)) return p;
+    if (v->cell_stride % 16 || v->n_head_kv > WS_CWARPS || v->cell_stride * WS_TILE_MAX > (1 << 20)) return p;
     if (v->n_cells % 4 || ((uintptr_t)v->pos & 15)) return p;
     if (c->fc != 64) return p;
     if (c->G != 1 && c->G != 2 && c->G != 4 && c->G != 5 && c->G != 6) return p;
     p.cell_bytes = (int)v->cell_stride;
-    p.tab_rows = v->pos_shared ? SC_T : SC_T * v->n_head_kv;
-    p.pos_ints = p.tab_rows;
     p.G = (int)c->G;
-    for (int ps = 2; ps >= 1; ps--)
-        for (int s = 4; s >= 2; s--) {
-            p.stages = s;
-            p.part_slots = ps;
-            if (p.total((int)c->fc) <= 220 * 1024) return p;
-        }
+    /* the largest tile, then the most partial buffers, then the most stages that fit */
+    for (int tile = c->G <= 4 ? WS_TILE_MAX : 16; tile >= 16; tile /= 2) {   /* 32 cells: too many registers above G = 4 */
+        p.tile = tile;
+        p.tab_rows = v->pos_shared ? tile : tile * v->n_head_kv;
+        p.pos_ints = p.tab_rows;
+        for (int ps = 2; ps >= 1; ps--)
+            for (int s = 4; s >= 2; s--) {
+                p.stages = s;
+                p.part_slots = ps;
+                if (p.total((int)c->fc) <= 220 * 1024) return p;
+            }
+    }
     p.stages = 0;
     return p;
 }
 
-template <int KT, int G>
+template <int KT, int G, int T>
 static int launch_ws_inst(const TmaScoreArgs &a, const WsPlan &plan, int grid, cudaStream_t st) {
-    auto fn = k_score_ws<KT, G>;
+    auto fn = k_score_ws<KT, G, T>;
     /* the setmaxnreg split inside the kernel assumes this launch allocation */
     static int regs = -1;
     if (regs < 0) {
@@ -463,12 +467,13 @@ static int launch_ws_inst(const TmaScoreArgs &a, const WsPlan &plan, int grid, c
 
 template <int KT>
 static int launch_ws_g(int G, const TmaScoreArgs &a, const WsPlan &plan, int grid, cudaStream_t st) {
+    const bool t32 = plan.tile == 32;
     switch (G) {
-        case 1: return launch_ws_inst<KT, 1>(a, plan, grid, st);
-        case 2: return launch_ws_inst<KT, 2>(a, plan, grid, st);
-        case 4: return launch_ws_inst<KT, 4>(a, plan, grid, st);
-        case 5: return launch_ws_inst<KT, 5>(a, plan, grid, st);
-        case 6: return launch_ws_inst<KT, 6>(a, plan, grid, st);
+        case 1: return t32 ? launch_ws_inst<KT, 1, 32>(a, plan, grid, st) : launch_ws_inst<KT, 1, 16>(a, plan, grid, st);
+        case 2: return t32 ? launch_ws_inst<KT, 2, 32>(a, plan, grid, st) : launch_ws_inst<KT, 2, 16>(a, plan, grid, st);
+        case 4: return t32 ? launch_ws_inst<KT, 4, 32>(a, plan, grid, st) : launch_ws_inst<KT, 4, 16>(a, plan, grid, st);
+        case 5: return launch_ws_inst<KT, 5, 16>(a, plan, grid, st);
+        case 6: return launch_ws_inst<KT, 6, 16>(a, plan, grid, st);
         default: FAIL(TRIA_ERR_UNSUPPORTED, "k_score_ws: gqa %d not instantiated", G);
     }
 }
@@ -506,7 +511,7 @@ static int launch_score_ws(tria_ctx *c, const tria_kv_view *v, const int32_t *n_
     a->raw = c->raw + (int64_t)l0 * KV * c->G * c->raw_stride;
     a->raw_stride = c->raw_stride;
     a->status = c->d_status;
-    a->tiles_per_layer = (max_rows + SC_T - 1) / SC_T;
+    a->tiles_per_layer = (max_rows + plan.tile - 1) / plan.tile;
     a->n_items = a->tiles_per_layer * nl;
     int rc = TRIA_OK;
     if (a->n_items > 0) {

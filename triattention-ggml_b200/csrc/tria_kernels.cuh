@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(SCORE_THREADS) k_score_raw(const ScoreArgs a) 
 /* ------------------------------------------------------------------ */
 
 constexpr int ST_TIMEOUT = 2;          /* status bit: a pipeline wait gave up */
-constexpr int SC_T = 16;               /* cells per work item (tile) */
+constexpr int WS_TILE_MAX = 32;        /* cells per work item: 32, or 16 when 32 does not fit */
 constexpr int WS_CWARPS = 8;           /* consumer warps: one kv head each */
 constexpr int WS_THREADS = (WS_CWARPS + 4) * 32;   /* + a producer warpgroup, one warp of it working */
 /* Register split (setmaxnreg): the CTA is launched with WS_LAUNCH_REGS per
@@ -266,7 +266,6 @@ static_assert(4 * 32 * WS_PRODUCER_REGS + WS_CWARPS * 32 * WS_CONSUMER_REGS <= W
               "register split exceeds the launch allocation");
 static_assert(WS_THREADS * WS_LAUNCH_REGS <= 65536, "launch allocation exceeds the register file");
 constexpr int WS_POS_RING = 8;         /* positions are fetched this many items ahead */
-constexpr int WS_CPL = 4;              /* cells per lane per pass: a warp's 16 cells at once */
 
 struct TmaScoreArgs {
     const uint8_t *k[TRIA_MAX_LAYERS];
@@ -289,13 +288,13 @@ struct TmaScoreArgs {
  * the consumers leave, for each of its rows, 8 lanes x GP partial sums
  * (GP = G padded to 4 or 8) in one of part_slots partial buffers. */
 struct WsPlan {
-    int stages, cell_bytes, tab_rows, pos_ints, G, part_slots;
+    int tile, stages, cell_bytes, tab_rows, pos_ints, G, part_slots;
     __host__ __device__ int gp() const { return G <= 4 ? 4 : 8; }
-    __host__ __device__ int k_bytes() const { return SC_T * cell_bytes; }
+    __host__ __device__ int k_bytes() const { return tile * cell_bytes; }
     __host__ __device__ int tab_bytes(int fc) const { return tab_rows * fc * 8; }
     __host__ __device__ int stage_bytes(int fc) const { return k_bytes() + tab_bytes(fc) + pos_ints * 4; }
     __host__ __device__ int ring_bytes() const { return WS_POS_RING * pos_ints * 4; }
-    __host__ __device__ int part_floats() const { return WS_CWARPS * SC_T * 8 * gp(); }   /* one buffer */
+    __host__ __device__ int part_floats() const { return WS_CWARPS * tile * 8 * gp(); }   /* one buffer */
     __host__ __device__ int total(int fc) const {
         return stages * stage_bytes(fc) + ring_bytes() + part_slots * part_floats() * 4 +
                (2 * stages + WS_POS_RING + 2 * part_slots) * 8;
@@ -394,7 +393,7 @@ __device__ __forceinline__ void row_pair(const uint8_t *row, int q, f2_t &kr, f2
  * Warp-specialised scoring (head_dim 128: fc = 64 frequencies, 32 pairs).
  *
  * Warp WS_CWARPS is the producer.  Positions of work item k arrive in a
- * small ring by bulk copy WS_POS_RING-1 items ahead.  For item k (a 16-cell
+ * small ring by bulk copy WS_POS_RING-1 items ahead.  For item k (a tile
  * tile of one layer; a CTA's items are contiguous) it waits until the
  * consumers released the stage, then bulk-copies (cp.async.bulk, no
  * multicast) the whole K tile in one copy and the delta-table rows
@@ -404,9 +403,10 @@ __device__ __forceinline__ void row_pair(const uint8_t *row, int q, f2_t &kr, f2
  * completes when all bytes landed.  Few large copies matter: the copy engine
  * streams 32 KB tiles at HBM speed but not sixteen 2 KB pieces.
  *
- * Each consumer warp scores one kv head, all 16 cells of the tile in one
- * pass: 8 lanes per cell, lane j owning the frequency pairs 8j..8j+7 (table
- * chunks 4j..4j+3) and WS_CPL = 4 cells, so a cell's 8 lanes load 128
+ * Each consumer warp scores one kv head, all cells of the tile (32, or 16
+ * when per-head table rows make a 32-cell stage too large) in one pass:
+ * 8 lanes per cell, lane j owning the frequency pairs 8j..8j+7 (table
+ * chunks 4j..4j+3) and SC_T / 4 cells, so a cell's 8 lanes load 128
  * contiguous bytes of K per instruction and, through the chunk rotation of
  * tab_chunk(), eight distinct bank groups of its table row.  The lane's
  * q-centre terms (pre-scaled by 1/17) and norm terms stay in registers for
@@ -419,9 +419,11 @@ __device__ __forceinline__ void row_pair(const uint8_t *row, int q, f2_t &kr, f2
  * code sits after its own setmaxnreg so the compiler budgets it alone.
  * Every wait is bounded (ST_TIMEOUT).
  */
-template <int KT, int G>
+template <int KT, int G, int SC_T>
 __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a, const WsPlan plan) {
     constexpr int FC = 64, NQ = FC / 2, QPL = 4;        /* pairs per lane */
+    constexpr int WS_CPL = SC_T / 4;                     /* cells per lane: a warp's tile cells in one pass */
+    static_assert(SC_T == 16 || SC_T == 32, "tile");
     extern __shared__ __align__(128) uint8_t smem[];
     const int KV = a.n_head_kv;
     const int S = plan.stages;
