@@ -37,3 +37,15 @@ def reflib():
 @pytest.fixture(scope="session")
 def synth_stats_path():
     return os.path.join(GOLDEN, "synth_l2h8kv4.tria")
+
+
+@pytest.fixture(scope="session")
+def torch_dev():
+    """cuda:0 with the library built; GPU tests fail (not skip) without a GPU."""
+    import torch
+    import tria_b200
+    if not torch.cuda.is_available():
+        pytest.fail("no CUDA device: the GPU tests need a B200")
+    if not os.path.exists(tria_b200.LIB_PATH):
+        tria_b200.build()
+    return torch.device("cuda:0")

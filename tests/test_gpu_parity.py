@@ -33,16 +33,6 @@ def assert_scores_close(got, ref, what=""):
                              f"gpu={got[i]!r} ref={ref[i]!r} |d|={d[i]:.3g}")
 
 
-@pytest.fixture(scope="module")
-def torch_dev():
-    import torch
-    if not torch.cuda.is_available():
-        pytest.fail("no CUDA device: the GPU tests need a B200")
-    if not os.path.exists(tria_b200.LIB_PATH):
-        tria_b200.build()
-    return torch.device("cuda:0")
-
-
 def _stats_file(tmp_path_factory, name, L, H, KV, hd, theta, seed, scales=None):
     p = str(tmp_path_factory.mktemp("stats") / name)
     workloads.write_tria(p, L, H, KV, hd, rope_theta=theta, seed=seed, scales=scales)
