@@ -623,42 +623,40 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
             uint8_t *sb = stages + st * stage_bytes;
             float4 *tab = reinterpret_cast<float4 *>(sb + plan.k_bytes());
             int32_t *slot = reinterpret_cast<int32_t *>(sb + plan.k_bytes() + plan.tab_bytes(FC));
-            /* Table rows per head row (or the shared row): one contiguous copy when
-             * the positions are consecutive (d falls by one per cell), else one
-             * copy per cell.  slot[] gets each (head, cell) row's table slot, or
-             * -1 when its delta is outside the table. */
+            /* Table rows per head row (or the shared row), one bulk copy per run of
+             * consecutive positions: a run of cells c..c+len-1 with positions
+             * p..p+len-1 needs table rows d-len+1..d (d = cur_pos - p), one
+             * contiguous range, copied into the run's own smem rows in ascending d.
+             * A fresh cache is one run per tile; a compacted cache keeps long
+             * runs (the recent window, clusters of kept rows).  slot[] gets each
+             * (head, cell) row's table row in the stage, or -1 when its delta is
+             * outside the table. */
             const int nrows = cells == 0 ? 0 : (a.pos_shared ? 1 : KV);
             const int32_t *rp = ring + (k % WS_POS_RING) * plan.pos_ints;
             for (int hh = 0; hh < nrows; hh++) {
                 const int32_t *hp = rp + hh * SC_T;
-                const int p0 = hp[0];
-                bool consec = true;
-                for (int c = lane; c < cells; c += 32) consec &= hp[c] == p0 + c;
-                consec = __all_sync(0xffffffffu, consec);
-                const int64_t dhi = (int64_t)a.cur_pos - p0 - a.t_lo;             /* row of cell 0 */
-                const int64_t dlo = dhi - (cells - 1);                             /* row of the last cell */
-                if (consec && dlo >= 0 && dhi < a.t_len) {
-                    if (lane < cells) slot[hh * SC_T + lane] = hh * SC_T + (cells - 1 - lane);
-                    if (lane == 0) {
-                        mbar_expect(&full[st], (uint32_t)cells * FC * 8);
-                        bulk_g2s(tab + hh * SC_T * NQ, a.table + dlo * NQ, (uint32_t)cells * FC * 8, &full[st]);
-                    }
-                } else {
-                    bool ok = false;
-                    int64_t di = 0;
-                    if (lane < cells) {
-                        di = (int64_t)a.cur_pos - hp[lane] - a.t_lo;
-                        ok = di >= 0 && di < a.t_len;
-                        slot[hh * SC_T + lane] = ok ? hh * SC_T + lane : -1;
-                    }
-                    const unsigned okm = __ballot_sync(0xffffffffu, ok);
-                    if (lane == 0) {
-                        mbar_expect(&full[st], (uint32_t)__popc(okm) * FC * 8);
-                        if (__popc(okm) != cells) atomicOr(a.status, ST_POSITION);
-                    }
-                    __syncwarp();
-                    if (ok) bulk_g2s(tab + (hh * SC_T + lane) * NQ, a.table + di * NQ, FC * 8, &full[st]);
+                const bool act = lane < cells;
+                const int p = act ? hp[lane] : 0;
+                const int64_t d = (int64_t)a.cur_pos - p - a.t_lo;
+                const bool ok = act && d >= 0 && d < a.t_len;
+                const int pprev = __shfl_up_sync(0xffffffffu, p, 1);
+                const bool okprev = __shfl_up_sync(0xffffffffu, ok ? 1 : 0, 1) != 0;
+                const bool cont = ok && lane > 0 && okprev && p == pprev + 1;
+                const bool start = ok && !cont;
+                const unsigned okm = __ballot_sync(0xffffffffu, ok);
+                const unsigned contm = __ballot_sync(0xffffffffu, cont);
+                const unsigned startm = __ballot_sync(0xffffffffu, start);
+                const unsigned after = lane < 31 ? contm >> (lane + 1) : 0u;
+                const int len = start ? __ffs(~after) : 0;         /* this run's cells, from its first lane */
+                if (start) {
+                    mbar_expect(&full[st], (uint32_t)len * FC * 8);
+                    bulk_g2s(tab + (hh * SC_T + lane) * NQ, a.table + (d - len + 1) * NQ, (uint32_t)len * FC * 8,
+                             &full[st]);
                 }
+                const int s0 = max(0, 31 - __clz(startm & ((2u << lane) - 1u)));   /* first lane of my run */
+                const int rl = __shfl_sync(0xffffffffu, len, s0);
+                if (act) slot[hh * SC_T + lane] = ok ? hh * SC_T + 2 * s0 + rl - 1 - lane : -1;
+                if (lane == 0 && __popc(okm) != cells) atomicOr(a.status, ST_POSITION);
                 __syncwarp();
             }
             if (lane == 0 && cells > 0) {
