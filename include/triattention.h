@@ -272,6 +272,39 @@ TRIA_API int tria_select_noalloc(const float *scores, int64_t score_stride,
                                  int32_t *kept_idx, int64_t kept_stride, int32_t *n_kept,
                                  void *stream);
 
+/* ---- Global budget across units (multi-sequence serving) ----
+ * New; the reference has no counterpart.  A sequence keeps its best K rows
+ * over all of its (layer, kv-head) units rather than a fixed count per unit:
+ * rows are ranked by (key desc, unit asc, row asc), key = tria_score_key(z)
+ * of the tria_score z-max scores, unit order = (layer, kv-head).  When the
+ * units of one sequence are split over ranks (contiguous layer blocks), the
+ * ranks agree on the threshold through these histograms, combined by the
+ * caller (an all-gather over the ranks and a sum):
+ *   1. tria_key_histogram(level 0) counts the keys' high 16 bits; summed over
+ *      ranks, the boundary bin b is the one where the count from the top
+ *      reaches K.
+ *   2. tria_key_histogram(level 1, prefix b) counts the low 16 bits of the
+ *      keys in bin b; summed, it gives the threshold key T and how many rows
+ *      equal to T are still needed.
+ *   3. tria_key_count(T) counts each unit's rows equal to T; rows equal to T
+ *      are kept in unit order, so a rank keeps what is left of the need after
+ *      the ranks holding earlier layers.
+ *   4. tria_select_key(T, counts, tie_allow) writes each unit's kept rows
+ *      (key > T, plus its share of the first tie_allow rows equal to T in unit
+ *      order) in ascending order; tria_compact then moves them.
+ * All pointers except n_rows are device memory; hist is [65536] uint32 and is
+ * added to (zero it first); counts is [units].  No context needed; each runs
+ * on the current device. */
+TRIA_API uint32_t tria_score_key(float score);
+TRIA_API int tria_key_histogram(const float *scores, int64_t score_stride, const int32_t *n_rows,
+                                int32_t units, int32_t level, uint32_t prefix, uint32_t *hist,
+                                void *stream);
+TRIA_API int tria_key_count(const float *scores, int64_t score_stride, const int32_t *n_rows,
+                            int32_t units, uint32_t key, int32_t *counts, void *stream);
+TRIA_API int tria_select_key(const float *scores, int64_t score_stride, const int32_t *n_rows,
+                             int32_t units, uint32_t key, const int32_t *counts, int64_t tie_allow,
+                             int32_t *kept_idx, int64_t kept_stride, int32_t *n_kept, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -241,3 +241,30 @@ def read_refc(path):
     expected = np.frombuffer(b[off:off + 4 * n], "<f4").copy()
     return dict(fc=fc, n=n, cur_pos=cur, layer=layer, kv_head=kvh, key_pos=key_pos,
                 k_re=k_re, k_im=k_im, expected=expected)
+
+
+# ---------------- global budget (multi-sequence) rule ----------------
+
+def score_keys(x):
+    """Order-preserving uint32 keys of fp32 scores, NaN lowest and -0 == +0
+    (the key oracle_score_key computes one value at a time)."""
+    x = np.asarray(x, np.float32).copy()
+    x[x == 0] = 0.0
+    u = x.view(np.uint32)
+    k = np.where(u & np.uint32(0x80000000), ~u, u | np.uint32(0x80000000)).astype(np.uint32)
+    k[np.isnan(x)] = 0
+    return k
+
+
+def global_select(keys_by_unit, k):
+    """The global-budget rule: keys_by_unit lists one uint32 key array per unit
+    in (layer, kv-head) order; returns per unit the kept row indices
+    (ascending) of the top k rows by (key desc, unit asc, row asc)."""
+    if not keys_by_unit:
+        return []
+    allk = np.concatenate([np.asarray(x, np.uint32) for x in keys_by_unit])
+    unit = np.concatenate([np.full(len(x), i, np.int64) for i, x in enumerate(keys_by_unit)])
+    row = np.concatenate([np.arange(len(x), dtype=np.int64) for x in keys_by_unit])
+    order = np.lexsort((row, unit, -allk.astype(np.int64)))
+    top = order[:max(0, min(k, allk.size))]
+    return [np.sort(row[top][unit[top] == i]) for i in range(len(keys_by_unit))]

@@ -1,0 +1,144 @@
+"""Global budget across units (multi-sequence serving), host logic on CPU.
+
+The orchestration in global_budget.py is run against a CPU stand-in for the
+three device calls (histogram, key count, select by key), in one process and
+on two gloo ranks that each own a contiguous block of layers; the kept sets
+must equal the oracle's global top-k with the (key desc, unit asc, row asc)
+rule, ties and NaN included.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import global_budget as gb
+import oracle_py
+
+
+class CpuBackend:
+    """Stand-in for DeviceBackend on numpy keys: seq = {"keys": [unit arrays]}."""
+
+    def histogram(self, seq, level, prefix):
+        import torch
+        h = np.zeros(gb.NBINS, np.int64)
+        for k in seq["keys"]:
+            k = np.asarray(k, np.uint32)
+            if level == 0:
+                np.add.at(h, (k >> 16).astype(np.int64), 1)
+            else:
+                sel = k[(k >> 16) == prefix]
+                np.add.at(h, (sel & 0xFFFF).astype(np.int64), 1)
+        return torch.from_numpy(h)
+
+    def count(self, seq, key):
+        import torch
+        seq["_counts"] = np.array([int((np.asarray(k, np.uint32) == key).sum()) for k in seq["keys"]], np.int64)
+        return torch.from_numpy(seq["_counts"])
+
+    def select(self, seq, key, tie_allow):
+        kept, before = [], 0
+        for k, c in zip(seq["keys"], seq["_counts"]):
+            k = np.asarray(k, np.uint32)
+            allow = max(0, min(tie_allow - before, int(c)))
+            eq = np.flatnonzero(k == key)[:allow]
+            kept.append(np.sort(np.concatenate([np.flatnonzero(k > key), eq])))
+            before += int(c)
+        seq["kept"] = kept
+
+
+def _make_seq_keys(rng, n_units, lo, hi, heavy_ties):
+    keys = []
+    for _ in range(n_units):
+        n = int(rng.integers(lo, hi + 1))
+        x = rng.standard_normal(n).astype(np.float32)
+        if heavy_ties:
+            x = (np.round(x * 2) / 2).astype(np.float32)
+            x[: n // 20] = np.nan
+        keys.append(oracle_py.score_keys(x))
+    return keys
+
+
+def test_boundary_bin():
+    h = np.zeros(gb.NBINS, np.int64)
+    h[[10, 500, 65535]] = [5, 3, 2]
+    assert gb.boundary_bin(h, 1) == (65535, 1)
+    assert gb.boundary_bin(h, 2) == (65535, 2)
+    assert gb.boundary_bin(h, 3) == (500, 1)
+    assert gb.boundary_bin(h, 5) == (500, 3)
+    assert gb.boundary_bin(h, 6) == (10, 1)
+    assert gb.boundary_bin(h, 10) == (10, 5)
+
+
+def test_score_keys_match_the_library():
+    import tria_b200
+    x = np.array([0.0, -0.0, 1.5, -1.5, np.inf, -np.inf, np.nan, 1e-40, -1e-40], np.float32)
+    assert [tria_b200.score_key(float(v)) for v in x] == oracle_py.score_keys(x).tolist()
+
+
+@pytest.mark.parametrize("heavy_ties", [False, True])
+def test_global_select_one_rank(heavy_ties):
+    import torch
+    rng = np.random.default_rng(3 + heavy_ties)
+    seqs, ks = [], []
+    for s in range(4):
+        keys = _make_seq_keys(rng, 12, 0 if s == 3 else 50, 400, heavy_ties)
+        seqs.append({"keys": keys})
+        ks.append([0, 17, 900, 10**6][s])
+    gb.global_select(seqs, ks, lambda t: t[None], CpuBackend(), 0)
+    for sq, k in zip(seqs, ks):
+        exp = oracle_py.global_select(sq["keys"], k)
+        assert len(sq["kept"]) == len(exp)
+        for a, b in zip(sq["kept"], exp):
+            assert np.array_equal(a, b)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(11)
+        all_seqs = [_make_seq_keys(rng, 16, 1, 300, s % 2 == 1) for s in range(3)]   # 16 units = 4 layers x 4 heads
+        ks = [100, 1234, 5000]
+        per = 16 // world
+        mine = [{"keys": keys[rank * per:(rank + 1) * per]} for keys in all_seqs]
+
+        def gather(t):
+            out = [torch.zeros_like(t) for _ in range(world)]
+            dist.all_gather(out, t.contiguous())
+            return torch.stack(out)
+
+        gb.global_select(mine, ks, gather, CpuBackend(), rank)
+        q.put((rank, [[k.tolist() for k in sq["kept"]] for sq in mine], [[k.tolist() for k in x] for x in all_seqs], ks))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_global_select_two_gloo_ranks():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    res.sort()
+    all_seqs, ks = res[0][2], res[0][3]
+    for s, keys in enumerate(all_seqs):
+        exp = oracle_py.global_select([np.array(k, np.uint32) for k in keys], ks[s])
+        got = res[0][1][s] + res[1][1][s]
+        assert len(got) == len(exp)
+        for a, b in zip(got, exp):
+            assert a == b.tolist()

@@ -823,6 +823,112 @@ extern "C" TRIA_API int tria_znorm_stats(const float *x, int64_t stride, const i
     return TRIA_OK;
 }
 
+/* ---- global budget ---- */
+
+static int key_args_check(const char *fn, const float *scores, int64_t stride, const int32_t *n_rows, int32_t units) {
+    if (!scores || !n_rows || units < 0) FAIL(TRIA_ERR_INVALID, "%s: null argument or negative units", fn);
+    for (int32_t u = 0; u < units; u++)
+        if (n_rows[u] < 0 || n_rows[u] > stride) FAIL(TRIA_ERR_INVALID, "%s: n_rows[%d] = %d outside [0, %lld]", fn, u,
+                                                    n_rows[u], (long long)stride);
+    return TRIA_OK;
+}
+
+template <class F>
+static int for_unit_chunks(int32_t units, F &&f) {
+    for (int32_t u0 = 0; u0 < units; u0 += TRIA_MAX_UNITS) {
+        const int rc = f(u0, std::min(TRIA_MAX_UNITS, units - u0));
+        if (rc) return rc;
+    }
+    return TRIA_OK;
+}
+
+extern "C" TRIA_API uint32_t tria_score_key(float x) {
+    if (x != x) return 0u;
+    if (x == 0.0f) x = 0.0f;
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+extern "C" TRIA_API int tria_key_histogram(const float *scores, int64_t score_stride, const int32_t *n_rows,
+                                           int32_t units, int32_t level, uint32_t prefix, uint32_t *hist,
+                                           void *stream) {
+    int rc = key_args_check("tria_key_histogram", scores, score_stride, n_rows, units);
+    if (rc) return rc;
+    if (!hist || (level != 0 && level != 1) || prefix > 0xffffu)
+        FAIL(TRIA_ERR_INVALID, "tria_key_histogram: hist NULL, level not 0/1 or prefix above 16 bits");
+    return for_unit_chunks(units, [&](int32_t u0, int32_t nu) -> int {
+        KeyArgs *a = new (std::nothrow) KeyArgs;
+        if (!a) FAIL(TRIA_ERR_NOMEM, "host allocation failed");
+        memset(a, 0, sizeof *a);
+        a->scores = scores + (int64_t)u0 * score_stride;
+        a->score_stride = score_stride;
+        a->units = nu;
+        a->level = level;
+        a->key = prefix;
+        a->hist = hist;
+        int mx = 0;
+        for (int u = 0; u < nu; u++) { a->n_rows[u] = n_rows[u0 + u]; mx = std::max(mx, a->n_rows[u]); }
+        if (mx > 0) k_key_hist<<<dim3((unsigned)std::min((mx + 255) / 256, 64), (unsigned)nu), 256, 0,
+                                 (cudaStream_t)stream>>>(*a);
+        delete a;
+        CUDA_TRY(cudaGetLastError());
+        return TRIA_OK;
+    });
+}
+
+extern "C" TRIA_API int tria_key_count(const float *scores, int64_t score_stride, const int32_t *n_rows,
+                                       int32_t units, uint32_t key, int32_t *counts, void *stream) {
+    int rc = key_args_check("tria_key_count", scores, score_stride, n_rows, units);
+    if (rc) return rc;
+    if (!counts) FAIL(TRIA_ERR_INVALID, "tria_key_count: counts NULL");
+    return for_unit_chunks(units, [&](int32_t u0, int32_t nu) -> int {
+        KeyArgs *a = new (std::nothrow) KeyArgs;
+        if (!a) FAIL(TRIA_ERR_NOMEM, "host allocation failed");
+        memset(a, 0, sizeof *a);
+        a->scores = scores + (int64_t)u0 * score_stride;
+        a->score_stride = score_stride;
+        a->units = nu;
+        a->key = key;
+        a->counts_out = counts + u0;
+        for (int u = 0; u < nu; u++) a->n_rows[u] = n_rows[u0 + u];
+        if (nu > 0) k_key_count<<<nu, SELECT_THREADS, 0, (cudaStream_t)stream>>>(*a);
+        delete a;
+        CUDA_TRY(cudaGetLastError());
+        return TRIA_OK;
+    });
+}
+
+extern "C" TRIA_API int tria_select_key(const float *scores, int64_t score_stride, const int32_t *n_rows,
+                                        int32_t units, uint32_t key, const int32_t *counts, int64_t tie_allow,
+                                        int32_t *kept_idx, int64_t kept_stride, int32_t *n_kept, void *stream) {
+    int rc = key_args_check("tria_select_key", scores, score_stride, n_rows, units);
+    if (rc) return rc;
+    if (!counts || !kept_idx || !n_kept) FAIL(TRIA_ERR_INVALID, "tria_select_key: null argument");
+    for (int32_t u = 0; u < units; u++)
+        if (n_rows[u] > kept_stride) FAIL(TRIA_ERR_INVALID, "tria_select_key: kept_stride below n_rows[%d]", u);
+    return for_unit_chunks(units, [&](int32_t u0, int32_t nu) -> int {
+        KeyArgs *a = new (std::nothrow) KeyArgs;
+        if (!a) FAIL(TRIA_ERR_NOMEM, "host allocation failed");
+        memset(a, 0, sizeof *a);
+        a->scores = scores + (int64_t)u0 * score_stride;
+        a->score_stride = score_stride;
+        a->units = nu;
+        a->key = key;
+        a->counts_in = counts;
+        a->u0 = u0;
+        a->tie_allow = tie_allow;
+        a->kept_idx = kept_idx + (int64_t)u0 * kept_stride;
+        a->kept_stride = kept_stride;
+        a->n_kept = n_kept + u0;
+        for (int u = 0; u < nu; u++) a->n_rows[u] = n_rows[u0 + u];
+        if (nu > 0) k_select_key<<<nu, SELECT_THREADS, 0, (cudaStream_t)stream>>>(*a);
+        delete a;
+        CUDA_TRY(cudaGetLastError());
+        return TRIA_OK;
+    });
+}
+
 extern "C" TRIA_API int tria_ctx_set_timing(tria_ctx *c, int enable) {
     if (!c) FAIL(TRIA_ERR_INVALID, "tria_ctx_set_timing: null ctx");
     DeviceGuard g(c->device);

@@ -1229,6 +1229,83 @@ __global__ void __launch_bounds__(SELECT_THREADS) k_select(const SelectArgs a) {
 }
 
 /* ------------------------------------------------------------------ */
+/* Global budget: one key threshold per sequence across its units       */
+/* ------------------------------------------------------------------ */
+/*
+ * A sequence keeps its best K rows over all of its (layer, kv-head) units,
+ * ranked by (key desc, unit asc, row asc) with the order-preserving key of
+ * the z-max score.  Ranks that own different layers agree on the threshold
+ * through histograms of the keys: 16-bit bins of the high half, then of the
+ * low half inside the boundary bin, then per-unit counts of rows equal to the
+ * threshold key, whose first `tie_allow` (in unit order) are kept too.
+ */
+struct KeyArgs {
+    const float *scores;
+    int64_t score_stride;
+    int32_t units, level;
+    uint32_t key;                     /* level 1: the high half; count / select: the threshold */
+    uint32_t *hist;                   /* [65536] */
+    const int32_t *counts_in;         /* select: per-unit threshold-key counts from unit 0 of the set */
+    int32_t *counts_out;              /* count: per-unit counts (this chunk) */
+    int32_t u0;                       /* first unit of this chunk within the set */
+    int64_t tie_allow;
+    int32_t *kept_idx;
+    int64_t kept_stride;
+    int32_t *n_kept;
+    int32_t n_rows[TRIA_MAX_UNITS];
+};
+
+__global__ void __launch_bounds__(256) k_key_hist(const KeyArgs a) {
+    const int u = blockIdx.y;
+    const int n = a.n_rows[u];
+    const float *sc = a.scores + (int64_t)u * a.score_stride;
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n; r += gridDim.x * blockDim.x) {
+        const uint32_t k = score_key(sc[r]);
+        if (a.level == 0) atomicAdd(&a.hist[k >> 16], 1u);
+        else if ((k >> 16) == a.key) atomicAdd(&a.hist[k & 0xffffu], 1u);
+    }
+}
+
+__global__ void __launch_bounds__(SELECT_THREADS) k_key_count(const KeyArgs a) {
+    __shared__ int s_warp[32];
+    const int u = blockIdx.x;
+    const int n = a.n_rows[u];
+    const float *sc = a.scores + (int64_t)u * a.score_stride;
+    int c = 0;
+    for (int r = threadIdx.x; r < n; r += blockDim.x) c += score_key(sc[r]) == a.key;
+    c = block_sum(c, s_warp);
+    if (threadIdx.x == 0) a.counts_out[u] = c;
+}
+
+__global__ void __launch_bounds__(SELECT_THREADS) k_select_key(const KeyArgs a) {
+    __shared__ int s_warp[32];
+    const int u = blockIdx.x, tid = threadIdx.x, bd = blockDim.x;
+    const int n = a.n_rows[u];
+    const float *sc = a.scores + (int64_t)u * a.score_stride;
+    int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
+    /* threshold-key rows of the units before this one (unit order = tie order) */
+    int before = 0;
+    for (int v = tid; v < a.u0 + u; v += bd) before += a.counts_in[v];
+    before = block_sum(before, s_warp);
+    const int64_t left = a.tie_allow - before;
+    const int allow = left <= 0 ? 0 : (int)min(left, (int64_t)a.counts_in[a.u0 + u]);
+    int run_eq = 0, run_kept = 0;
+    for (int base = 0; base < n; base += bd) {
+        const int r = base + tid;
+        const uint32_t k = r < n ? score_key(sc[r]) : 0u;
+        const bool eq = r < n && k == a.key;
+        int tot_eq, tot_k;
+        const int eq_rank = run_eq + block_excl_scan(eq, s_warp, tot_eq);
+        const bool kp = r < n && (k > a.key || (eq && eq_rank < allow));
+        const int dst = run_kept + block_excl_scan(kp, s_warp, tot_k);
+        if (kp) kept[dst] = r;
+        run_eq += tot_eq;
+        run_kept += tot_k;
+    }
+    if (tid == 0) a.n_kept[u] = run_kept;
+}
+
+/* ------------------------------------------------------------------ */
 /* Compaction                                                           */
 /* ------------------------------------------------------------------ */
 

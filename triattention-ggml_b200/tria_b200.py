@@ -113,6 +113,14 @@ def lib() -> C.CDLL:
                                           C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
                                           C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]
         L.tria_znorm_stats.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]
+        L.tria_score_key.restype = C.c_uint32
+        L.tria_score_key.argtypes = [C.c_float]
+        L.tria_key_histogram.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int32, C.c_int32, C.c_uint32,
+                                         C.c_void_p, C.c_void_p]
+        L.tria_key_count.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int32, C.c_uint32, C.c_void_p,
+                                     C.c_void_p]
+        L.tria_select_key.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int32, C.c_uint32, C.c_void_p,
+                                      C.c_int64, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]
         L.tria_score_kv_head_dev.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
                                              C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]
         _lib = L
@@ -176,6 +184,35 @@ def znorm_stats(x, stride, n, mean_std, stream=None):
     nn = np.ascontiguousarray(n, np.int32)
     check(lib().tria_znorm_stats(_ptr(x), int(stride), nn.ctypes.data, int(nn.shape[0]),
                                  _ptr(mean_std), _stream(stream)))
+
+
+def score_key(x: float) -> int:
+    """tria_score_key: the order-preserving 32-bit key of a score."""
+    return int(lib().tria_score_key(float(x)))
+
+
+def key_histogram(scores, score_stride, n_rows, level, prefix, hist, stream=None):
+    """tria_key_histogram: add the 16-bit bins of the keys of device `scores`
+    ([units][score_stride]) to device `hist` [65536] uint32."""
+    nr = np.ascontiguousarray(n_rows, np.int32)
+    check(lib().tria_key_histogram(_ptr(scores), int(score_stride), nr.ctypes.data, int(nr.shape[0]),
+                                   int(level), int(prefix), _ptr(hist), _stream(stream)))
+
+
+def key_count(scores, score_stride, n_rows, key, counts, stream=None):
+    """tria_key_count: per-unit counts of rows whose key equals `key`."""
+    nr = np.ascontiguousarray(n_rows, np.int32)
+    check(lib().tria_key_count(_ptr(scores), int(score_stride), nr.ctypes.data, int(nr.shape[0]),
+                               int(key), _ptr(counts), _stream(stream)))
+
+
+def select_key(scores, score_stride, n_rows, key, counts, tie_allow, kept_idx, kept_stride, n_kept, stream=None):
+    """tria_select_key: keep rows with key > `key` and the first `tie_allow`
+    rows equal to it (unit order), kept indices ascending per unit."""
+    nr = np.ascontiguousarray(n_rows, np.int32)
+    check(lib().tria_select_key(_ptr(scores), int(score_stride), nr.ctypes.data, int(nr.shape[0]), int(key),
+                                _ptr(counts), int(tie_allow), _ptr(kept_idx), int(kept_stride), _ptr(n_kept),
+                                _stream(stream)))
 
 
 def select_noalloc(scores, score_stride, n_rows, keep, kept_idx, kept_stride, n_kept,
