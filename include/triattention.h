@@ -206,6 +206,20 @@ TRIA_API int tria_evict(tria_ctx *ctx, const struct tria_kv_view *src,
                         const struct tria_evict_params *params, int32_t *n_kept_out,
                         void *stream);
 
+/* tria_evict for a cache that lives in host memory (an offloaded KV cache, or
+ * the reference's CPU buffers).  src and dst views hold HOST pointers into
+ * page-locked memory (cudaHostAlloc, or cudaHostRegister'ed): K streams to the
+ * device in chunks of layers (copy engine, double-buffered against the
+ * scoring), V is read by the device only for the rows it keeps, and the kept
+ * K, V and positions are written straight into dst.  dst needs room for the
+ * kept rows only (keep + window + sink per unit).  The call returns once the
+ * work is queued on `stream`; the host buffers must stay untouched until
+ * tria_get_n_kv() (which waits) returns.  Pageable memory is refused with
+ * TRIA_ERR_INVALID.  New. */
+TRIA_API int tria_evict_host(tria_ctx *ctx, const struct tria_kv_view *src,
+                             const struct tria_kv_view *dst, const int32_t *n_rows,
+                             const struct tria_evict_params *params, void *stream);
+
 /* Rows per (layer, head) after the last tria_evict on `ctx` (waits for it):
  * writes the per-unit counts to n_kept (host, may be NULL; `cap` entries at
  * most) and returns their maximum, the cache length a llama.cpp runtime must

@@ -105,6 +105,15 @@ struct tria_ctx {
     cudaEvent_t ev_stage[6] = {};
     int64_t launches = 0;
     std::mutex mu;
+    /* tria_evict_host: double-buffered device staging of K (and positions) */
+    cudaStream_t copy_stream = nullptr;
+    uint8_t *hs_k[2] = {nullptr, nullptr};
+    int32_t *hs_pos[2] = {nullptr, nullptr};
+    size_t hs_k_cap = 0, hs_pos_cap = 0;
+    cudaEvent_t hs_copied[2] = {nullptr, nullptr}, hs_freed[2] = {nullptr, nullptr};
+    bool hs_used[2] = {false, false};
+    int32_t *d_cnt_all = nullptr;
+    int64_t cnt_all_cap = 0;
 };
 
 static int check_device(int device) {
@@ -136,6 +145,14 @@ extern "C" TRIA_API void tria_ctx_destroy(tria_ctx *ctx) {
         if (ctx->ev_done) cudaEventDestroy(ctx->ev_done);
         for (cudaEvent_t e : ctx->ev_stage) if (e) cudaEventDestroy(e);
         if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+        if (ctx->copy_stream) { cudaStreamSynchronize(ctx->copy_stream); cudaStreamDestroy(ctx->copy_stream); }
+        for (int b = 0; b < 2; b++) {
+            cudaFree(ctx->hs_k[b]);
+            cudaFree(ctx->hs_pos[b]);
+            if (ctx->hs_copied[b]) cudaEventDestroy(ctx->hs_copied[b]);
+            if (ctx->hs_freed[b]) cudaEventDestroy(ctx->hs_freed[b]);
+        }
+        cudaFree(ctx->d_cnt_all);
     }
     delete ctx;
 }
@@ -820,6 +837,163 @@ extern "C" TRIA_API int tria_znorm_stats(const float *x, int64_t stride, const i
         for (int i = 0; i < cn; i++) z.n_rows[i] = n[c0 + i];
         CUDA_TRY(znorm_walk_launch(z, cn, (cudaStream_t)stream));
     }
+    return TRIA_OK;
+}
+
+/* ---- host-resident caches ---- */
+
+/* Page-locked (or managed / device) memory that kernels may read and write
+ * through its own address.  Unregistered pageable memory is refused: a kernel
+ * touching it would fault. */
+static bool device_accessible(const void *p) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) { cudaGetLastError(); return false; }
+    return at.type == cudaMemoryTypeHost || at.type == cudaMemoryTypeManaged || at.type == cudaMemoryTypeDevice;
+}
+
+static int check_range(const void *base, size_t bytes, const char *what, int l) {
+    if (!bytes) return TRIA_OK;
+    if (!device_accessible(base) || !device_accessible((const uint8_t *)base + bytes - 1))
+        FAIL(TRIA_ERR_INVALID, "tria_evict_host: %s[%d] is not page-locked host memory (cudaHostAlloc / "
+             "cudaHostRegister) nor device memory", what, l);
+    return TRIA_OK;
+}
+
+extern "C" TRIA_API int tria_evict_host(tria_ctx *c, const tria_kv_view *s, const tria_kv_view *d,
+                                        const int32_t *n_rows, const tria_evict_params *p, void *stream) {
+    if (!c || !n_rows || !p) FAIL(TRIA_ERR_INVALID, "tria_evict_host: null argument");
+    int rc = validate_view(c, s, n_rows, "tria_evict_host src", false);
+    if (!rc) rc = validate_view(c, d, nullptr, "tria_evict_host dst", false);
+    if (!rc) rc = check_pair(s, d);
+    if (rc) return rc;
+    const int KV = s->n_head_kv;
+    const int64_t units = (int64_t)s->n_layer * KV;
+    DeviceGuard g(c->device);
+    std::vector<int32_t> keep;
+    keep_requests(c, s, n_rows, p, keep);
+    const int extra = (p->window > 0 ? p->window : 0) + (p->sink > 0 ? p->sink : 0);
+    int max_rows = 0;
+    for (int64_t u = 0; u < units; u++) {
+        max_rows = std::max(max_rows, n_rows[u]);
+        /* dst holds the kept rows: at most keep + protected rows */
+        const int64_t bound = std::min<int64_t>(n_rows[u], (int64_t)keep[u] + extra);
+        if (bound > d->n_cells) FAIL(TRIA_ERR_INVALID, "tria_evict_host: dst n_cells %d < %lld kept rows possible in unit %lld",
+                                     d->n_cells, (long long)bound, (long long)u);
+    }
+    /* every buffer the device touches must be reachable from it */
+    const int64_t cs = s->cell_stride;
+    for (int l = 0; l < s->n_layer; l++) {
+        if ((rc = check_range(s->k[l], (size_t)max_rows * cs, "src k", l))) return rc;
+        if (s->v && (rc = check_range(s->v[l], (size_t)max_rows * cs, "src v", l))) return rc;
+        if ((rc = check_range(d->k[l], (size_t)d->n_cells * d->cell_stride, "dst k", l))) return rc;
+        if (d->v && (rc = check_range(d->v[l], (size_t)d->n_cells * d->cell_stride, "dst v", l))) return rc;
+    }
+    if ((rc = check_range(s->pos, (size_t)(s->pos_shared ? 1 : units) * s->n_cells * 4, "src pos", 0))) return rc;
+    if ((rc = check_range(d->pos, (size_t)units * d->n_cells * 4, "dst pos", 0))) return rc;
+
+    cudaStream_t st = (cudaStream_t)stream;
+    if (!c->copy_stream) CUDA_TRY(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
+    for (int b = 0; b < 2; b++) {
+        if (!c->hs_copied[b]) CUDA_TRY(cudaEventCreateWithFlags(&c->hs_copied[b], cudaEventDisableTiming));
+        if (!c->hs_freed[b]) CUDA_TRY(cudaEventCreateWithFlags(&c->hs_freed[b], cudaEventDisableTiming));
+    }
+    /* chunks of lc layers, staged in two device buffers */
+    const int lc = std::max(1, std::min({s->n_layer, 4, TRIA_MAX_UNITS / KV}));
+    const size_t kb = (size_t)lc * s->n_cells * cs;
+    const size_t pb = (size_t)(s->pos_shared ? 1 : lc * KV) * s->n_cells * 4;
+    if (kb > c->hs_k_cap || pb > c->hs_pos_cap) {
+        cudaDeviceSynchronize();
+        for (int b = 0; b < 2; b++) {
+            cudaFree(c->hs_k[b]); c->hs_k[b] = nullptr;
+            cudaFree(c->hs_pos[b]); c->hs_pos[b] = nullptr;
+            c->hs_used[b] = false;
+        }
+        c->hs_k_cap = c->hs_pos_cap = 0;
+        for (int b = 0; b < 2; b++) {
+            CUDA_TRY(cudaMalloc(&c->hs_k[b], kb));
+            CUDA_TRY(cudaMalloc(&c->hs_pos[b], pb));
+        }
+        c->hs_k_cap = kb;
+        c->hs_pos_cap = pb;
+    }
+    if (units > c->cnt_all_cap) {
+        cudaDeviceSynchronize();
+        cudaFree(c->d_cnt_all);
+        c->d_cnt_all = nullptr;
+        c->cnt_all_cap = 0;
+        CUDA_TRY(cudaMalloc(&c->d_cnt_all, (size_t)units * 4));
+        c->cnt_all_cap = units;
+    }
+    if ((rc = check_positions_range(c, p->cur_pos, st))) return rc;
+    if ((rc = ensure_scratch(c, (int64_t)lc * KV, s->n_cells, st))) return rc;
+    /* the host may reuse its buffers for the next step once this one is done:
+     * the copy stream starts after the compute stream's earlier work */
+    cudaEvent_t start = nullptr;
+    CUDA_TRY(cudaEventCreateWithFlags(&start, cudaEventDisableTiming));
+    CUDA_TRY(cudaEventRecord(start, st));
+    CUDA_TRY(cudaStreamWaitEvent(c->copy_stream, start, 0));
+    cudaEventDestroy(start);
+
+    for (int l0 = 0, ci = 0; l0 < s->n_layer; l0 += lc, ci++) {
+        const int b = ci & 1, nl = std::min(lc, s->n_layer - l0);
+        const int64_t u0 = (int64_t)l0 * KV;
+        if (c->hs_used[b]) CUDA_TRY(cudaStreamWaitEvent(c->copy_stream, c->hs_freed[b], 0));
+        void *kptr[TRIA_MAX_LAYERS], *vptr[TRIA_MAX_LAYERS], *dk[TRIA_MAX_LAYERS], *dvp[TRIA_MAX_LAYERS];
+        for (int l = 0; l < nl; l++) {
+            int lr = 0;
+            for (int h = 0; h < KV; h++) lr = std::max(lr, n_rows[u0 + (int64_t)l * KV + h]);
+            uint8_t *dst_k = c->hs_k[b] + (size_t)l * s->n_cells * cs;
+            if (lr) CUDA_TRY(cudaMemcpyAsync(dst_k, s->k[l0 + l], (size_t)lr * cs, cudaMemcpyDefault, c->copy_stream));
+            kptr[l] = dst_k;
+            vptr[l] = s->v ? s->v[l0 + l] : nullptr;
+            dk[l] = d->k[l0 + l];
+            dvp[l] = d->v ? d->v[l0 + l] : nullptr;
+        }
+        const int32_t *src_pos = s->pos_shared ? s->pos : s->pos + u0 * s->n_cells;
+        const size_t pos_b = (size_t)(s->pos_shared ? 1 : nl * KV) * s->n_cells * 4;
+        CUDA_TRY(cudaMemcpyAsync(c->hs_pos[b], src_pos, pos_b, cudaMemcpyDefault, c->copy_stream));
+        CUDA_TRY(cudaEventRecord(c->hs_copied[b], c->copy_stream));
+        CUDA_TRY(cudaStreamWaitEvent(st, c->hs_copied[b], 0));
+        tria_kv_view dv = *s;                             /* K and positions on the device, V in host memory */
+        dv.n_layer = nl;
+        dv.layer0 = s->layer0 + l0;
+        dv.k = kptr;
+        dv.v = s->v ? vptr : nullptr;
+        dv.pos = c->hs_pos[b];
+        tria_kv_view dd = *d;                             /* kept rows straight into host memory */
+        dd.n_layer = nl;
+        dd.layer0 = d->layer0 + l0;
+        dd.k = dk;
+        dd.v = d->v ? dvp : nullptr;
+        dd.pos = d->pos + u0 * d->n_cells;
+        const int32_t *nr = n_rows + u0;
+        std::vector<int32_t> kc(keep.begin() + u0, keep.begin() + u0 + (int64_t)nl * KV);
+        int32_t *cnt = c->d_cnt_all + u0;
+        if ((rc = run_score(c, &dv, nr, p->cur_pos, s->type, st))) return rc;
+        if ((rc = run_znorm(c, &dv, nr, st))) return rc;
+        if ((rc = launch_select(c, &dv, nr, kc, p, true, nullptr, c->kept, c->cell_stride, cnt, st))) return rc;
+        int hint = 0;
+        for (int32_t k : kc) hint = std::max(hint, k);
+        if (extra) hint += extra + 1;
+        if ((rc = launch_compact(c, &dv, &dd, nr, c->kept, c->cell_stride, cnt, st, hint))) return rc;
+        CUDA_TRY(cudaEventRecord(c->hs_freed[b], st));
+        c->hs_used[b] = true;
+    }
+    c->have_timing = false;
+    CUDA_TRY(cudaMemcpyAsync(c->h_pinned, c->d_status, 4, cudaMemcpyDeviceToHost, st));
+    if (c->pinned_cap < units + 1) {
+        cudaStreamSynchronize(st);
+        if (c->h_pinned) cudaFreeHost(c->h_pinned);
+        c->h_pinned = nullptr;
+        c->pinned_cap = 0;
+        CUDA_TRY(cudaMallocHost(&c->h_pinned, (size_t)(units + 1) * 4));
+        c->pinned_cap = (int32_t)(units + 1);
+        CUDA_TRY(cudaMemcpyAsync(c->h_pinned, c->d_status, 4, cudaMemcpyDeviceToHost, st));
+    }
+    CUDA_TRY(cudaMemcpyAsync(c->h_pinned + 1, c->d_cnt_all, (size_t)units * 4, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaEventRecord(c->ev_done, st));
+    c->last_units = (int32_t)units;
+    c->have_step = true;
     return TRIA_OK;
 }
 

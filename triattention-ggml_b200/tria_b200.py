@@ -105,6 +105,8 @@ def lib() -> C.CDLL:
         L.tria_evict.argtypes = [C.c_void_p, C.POINTER(KvView), C.POINTER(KvView), C.c_void_p,
                                  C.POINTER(EvictParams), C.c_void_p, C.c_void_p]
         L.tria_get_n_kv.argtypes = [C.c_void_p, C.c_void_p, C.c_int32]
+        L.tria_evict_host.argtypes = [C.c_void_p, C.POINTER(KvView), C.POINTER(KvView), C.c_void_p,
+                                      C.POINTER(EvictParams), C.c_void_p]
         L.tria_ctx_set_timing.argtypes = [C.c_void_p, C.c_int]
         L.tria_ctx_stage_ms.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
         L.tria_ctx_launches.restype = C.c_int64
@@ -300,6 +302,11 @@ class Context:
         a, p = self._rows(n_rows)
         check(lib().tria_evict(self.h, C.byref(src), C.byref(dst), p, C.byref(params),
                                _ptr(n_kept_out), _stream(stream)))
+
+    def evict_host(self, src, dst, n_rows, params, stream=None):
+        """tria_evict_host: src/dst views over page-locked host buffers."""
+        a, p = self._rows(n_rows)
+        check(lib().tria_evict_host(self.h, C.byref(src), C.byref(dst), p, C.byref(params), _stream(stream)))
 
     def get_n_kv(self, units: int = 0):
         buf = np.zeros(max(units, 1), np.int32)
