@@ -436,6 +436,10 @@ static int launch_znorm(tria_ctx *c, int64_t unit0, int units, const int32_t *n_
 /* Shared-memory plan of k_score_ws for this view; stages == 0 when the view
  * does not qualify (cell tiles must be contiguous 16-byte multiples, <= 8 kv
  * heads, head_dim 128, positions 16-byte aligned with n_cells % 4 == 0). */
+/* Dynamic shared memory of one k_score_ws block: the sm_100 opt-in maximum
+ * (227 KB) less a little for the kernel's static shared variables. */
+static constexpr int WS_SMEM_MAX = 232448 - 256;
+
 static WsPlan ws_plan(const tria_ctx *c, const tria_kv_view *v) {
     WsPlan p{};
     const int64_t rb = view_row_bytes(v->type, (int)c->hd);
@@ -455,7 +459,7 @@ static WsPlan ws_plan(const tria_ctx *c, const tria_kv_view *v) {
             for (int s = 4; s >= 2; s--) {
                 p.stages = s;
                 p.part_slots = ps;
-                if (p.total((int)c->fc) <= 220 * 1024) return p;
+                if (p.total((int)c->fc) <= WS_SMEM_MAX) return p;
             }
     }
     p.stages = 0;
