@@ -146,8 +146,17 @@ struct tria_kv_view {
     void * const *v;        /* host array [n_layer] of device pointers, or NULL (K only) */
     int32_t *pos;           /* device */
     int32_t  pos_shared;
-    int32_t  reserved;
+    int32_t  flags;         /* TRIA_VIEW_* bits, 0 for a cache of pre-RoPE keys */
 };
+
+/* The cache stores keys after RoPE, as llama.cpp does: NeoX pairing (dims f
+ * and f + head_dim/2), k_post = s * e^{i*theta} * k_pre with theta =
+ * fl(pos * omega_f) in fp32 (omega of the stats) and s the stats'
+ * attn_scale (rope attention scaling).  Scoring undoes the rotation exactly
+ * in the table it reads (triattention_validate_rope.py:17-28 inverts it the
+ * same way in torch); selection and compaction are unchanged.  The angle must
+ * be the one the cache's RoPE used for scores to match pre-RoPE scoring. */
+#define TRIA_VIEW_POST_ROPE 1
 
 /* Eviction policy of one step.  The kept count of a (layer, kv-head) with n
  * rows is  B_l = tria_layer_budget(stats, layer, budget),

@@ -74,6 +74,11 @@ struct tria_ctx {
     int device = 0;
     uint32_t L = 0, H = 0, KV = 0, hd = 0, fc = 0, G = 0;
     std::vector<float> scales;           /* layer budget scales (host) */
+    float attn_scale = 1.0f;             /* rope attention scaling of the stats (post-RoPE keys) */
+    /* position table for post-RoPE views: rows p in [0, ptab_cur] of trigger ptab_cur */
+    float2 *d_ptab = nullptr;
+    int64_t ptab_cap = 0, ptab_cur = -1;
+    int64_t ptab_t_lo = 0, ptab_t_len = 0;
     float *d_q = nullptr;                /* [L][H][3][fc] */
     float *d_omega = nullptr;            /* [fc] */
     /* delta table: entries for d in [t_lo, t_lo + t_len), capacity t_cap rows */
@@ -138,6 +143,7 @@ extern "C" TRIA_API void tria_ctx_destroy(tria_ctx *ctx) {
         cudaFree(ctx->d_q);
         cudaFree(ctx->d_omega);
         cudaFree(ctx->d_table);
+        cudaFree(ctx->d_ptab);
         cudaFree(ctx->d_scratch);
         cudaFree(ctx->d_io);
         cudaFree(ctx->d_status);
@@ -177,6 +183,7 @@ extern "C" TRIA_API int tria_ctx_create(const tria_stats *s, int device, tria_ct
     c->L = s->num_layers; c->H = s->num_heads; c->KV = s->num_kv_heads;
     c->hd = s->head_dim; c->fc = s->freq_count; c->G = G;
     c->scales.assign(s->layer_budget_scales, s->layer_budget_scales + s->num_layers);
+    c->attn_scale = s->attn_scale;
     const size_t fc = c->fc;
     std::vector<float> q((size_t)c->L * c->H * 3 * fc);
     for (size_t h = 0; h < (size_t)c->L * c->H; h++) {
@@ -307,6 +314,7 @@ static int validate_view(const tria_ctx *c, const tria_kv_view *v, const int32_t
         FAIL(TRIA_ERR_INVALID, "%s: kv heads [%d, %d) outside the stats' %u", what, v->head0,
              v->head0 + v->n_head_kv, c->KV);
     if (v->n_cells < 0) FAIL(TRIA_ERR_INVALID, "%s: negative n_cells", what);
+    if (v->flags & ~TRIA_VIEW_POST_ROPE) FAIL(TRIA_ERR_INVALID, "%s: unknown view flags 0x%x", what, v->flags);
     if (!v->k || !v->pos) FAIL(TRIA_ERR_INVALID, "%s: null k or pos", what);
     if (need_v && !v->v) FAIL(TRIA_ERR_INVALID, "%s: null v", what);
     if ((v->cell_stride & 3) || (v->head_stride & 3) || v->cell_stride <= 0 || v->head_stride < 0)
@@ -390,9 +398,12 @@ static void fill_score_args(const tria_ctx *c, const tria_kv_view *v, const int3
     a.H = (int32_t)c->H;
     a.fc = (int32_t)c->fc;
     a.q = c->d_q;
-    a.table = c->d_table;
-    a.t_lo = c->t_lo;
-    a.t_len = c->t_len;
+    const bool post = (v->flags & TRIA_VIEW_POST_ROPE) != 0;
+    a.table = post ? c->d_ptab : c->d_table;
+    a.t_lo = post ? 0 : c->t_lo;
+    a.t_len = post ? (int64_t)cur_pos + 1 : c->t_len;
+    a.by_pos = post ? 1 : 0;
+    a.qx_scale = post ? 1.0f / c->attn_scale : 1.0f;
     a.raw = c->raw + (int64_t)l0 * v->n_head_kv * c->G * c->raw_stride;
     a.raw_stride = c->raw_stride;
     a.status = c->d_status;
@@ -526,9 +537,12 @@ static int launch_score_ws(tria_ctx *c, const tria_kv_view *v, const int32_t *n_
     a->cur_pos = cur_pos;
     a->H = (int32_t)c->H;
     a->q = c->d_q;
-    a->table = reinterpret_cast<const float4 *>(c->d_table);
-    a->t_lo = c->t_lo;
-    a->t_len = c->t_len;
+    const bool post = (v->flags & TRIA_VIEW_POST_ROPE) != 0;
+    a->table = reinterpret_cast<const float4 *>(post ? c->d_ptab : c->d_table);
+    a->t_lo = post ? 0 : c->t_lo;
+    a->t_len = post ? (int64_t)cur_pos + 1 : c->t_len;
+    a->by_pos = post ? 1 : 0;
+    a->qx_scale = post ? 1.0f / c->attn_scale : 1.0f;
     a->raw = c->raw + (int64_t)l0 * KV * c->G * c->raw_stride;
     a->raw_stride = c->raw_stride;
     a->status = c->d_status;
@@ -546,8 +560,14 @@ static int launch_score_ws(tria_ctx *c, const tria_kv_view *v, const int32_t *n_
 }
 
 /* Raw scores of every unit of `v`. */
+static int ensure_ptab(tria_ctx *c, int32_t cur_pos, cudaStream_t st);
+
 static int run_score(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, int32_t cur_pos, int kt,
                      cudaStream_t st) {
+    if (v->flags & TRIA_VIEW_POST_ROPE) {
+        const int rc = ensure_ptab(c, cur_pos, st);
+        if (rc) return rc;
+    }
     const WsPlan plan = kt == KT_F32SPLIT ? WsPlan{} : ws_plan(c, v);
     if (plan.stages > 0) {
         return for_layer_chunks(v, [&](int l0, int nl) -> int {
@@ -690,6 +710,36 @@ static int launch_compact(tria_ctx *c, const tria_kv_view *s, const tria_kv_view
 static int check_positions_range(tria_ctx *c, int32_t cur_pos, cudaStream_t st) {
     if (cur_pos < 0) FAIL(TRIA_ERR_INVALID, "cur_pos %d < 0", cur_pos);
     return ensure_table(c, 0, cur_pos, st);
+}
+
+/* The position table of trigger position cur_pos (k_build_ptab), rebuilt when
+ * cur_pos, the delta table or the rope scaling it folds in changes. */
+static int ensure_ptab(tria_ctx *c, int32_t cur_pos, cudaStream_t st) {
+    int rc = check_positions_range(c, cur_pos, st);
+    if (rc) return rc;
+    if (!(c->attn_scale > 0.0f) || !std::isfinite(c->attn_scale))
+        FAIL(TRIA_ERR_INVALID, "post-RoPE keys need a positive finite attn_scale in the stats (got %g)",
+             (double)c->attn_scale);
+    if (c->ptab_cur == cur_pos && c->ptab_t_lo == c->t_lo && c->ptab_t_len == c->t_len) return TRIA_OK;
+    const int64_t rows = (int64_t)cur_pos + 1, fc = c->fc;
+    if (rows > c->ptab_cap) {
+        cudaStreamSynchronize(st);
+        cudaFree(c->d_ptab);
+        c->d_ptab = nullptr;
+        c->ptab_cap = 0;
+        const int64_t cap = std::max<int64_t>(rows + rows / 4, 4096);
+        CUDA_TRY(cudaMalloc(&c->d_ptab, (size_t)cap * fc * sizeof(float2)));
+        c->ptab_cap = cap;
+    }
+    const int64_t total = rows * fc;
+    k_build_ptab<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(c->d_ptab, c->d_table, c->t_lo, cur_pos,
+                                                                  c->d_omega, (int)fc, 1.0f / c->attn_scale);
+    CUDA_TRY(cudaGetLastError());
+    c->launches++;
+    c->ptab_cur = cur_pos;
+    c->ptab_t_lo = c->t_lo;
+    c->ptab_t_len = c->t_len;
+    return TRIA_OK;
 }
 
 extern "C" TRIA_API int tria_score(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, int32_t cur_pos,
@@ -1158,6 +1208,8 @@ static int score_split(tria_ctx *c, const float *k_re, const float *k_im, const 
     a->table = c->d_table;
     a->t_lo = c->t_lo;
     a->t_len = c->t_len;
+    a->by_pos = 0;
+    a->qx_scale = 1.0f;
     a->raw = c->raw;
     a->raw_stride = c->raw_stride;
     a->status = c->d_status;

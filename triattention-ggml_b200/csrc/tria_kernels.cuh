@@ -87,6 +87,31 @@ __global__ void k_build_table(float2 *__restrict__ T, int64_t d_lo, int64_t n_d,
     Tf[2] = (float)s;
 }
 
+/* Position table for post-RoPE keys.  A cache that stores keys after NeoX
+ * RoPE (pairs (f, f + fc), k_post = s * e^{i*theta_p} * k_pre, theta_p =
+ * fl(p * omega_f) in fp32, s the rope scaling) is scored by folding the
+ * inverse rotation into the delta table: the rotation the score applies to a
+ * pre-RoPE key, (C - iS) of delta d = cur - p, times e^{-i*theta_p} / s, is one
+ * table row per position for this trigger position:
+ *   P[p] = ((C cos - S sin) / s,  (S cos + C sin) / s),  (C, S) = T[cur - p].
+ * Evaluated in double from the fp32 angle; same chunk layout as T. */
+__global__ void k_build_ptab(float2 *__restrict__ P, const float2 *__restrict__ T, int64_t t_lo, int64_t cur,
+                             const float *__restrict__ omega, int fc, float inv_scale) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i > cur * fc + fc - 1) return;
+    const int64_t p = i / fc;
+    const int f = (int)(i - p * fc);
+    const int off = 4 * tab_chunk(f >> 1) + (f & 1);
+    const float *Tf = reinterpret_cast<const float *>(T) + (cur - p - t_lo) * 2 * fc + off;
+    const double C = Tf[0], S = Tf[2];
+    const float ang = __fmul_rn((float)p, omega[f]);
+    double sn, cs;
+    sincos((double)ang, &sn, &cs);
+    float *Pf = reinterpret_cast<float *>(P) + p * 2 * fc + off;
+    Pf[0] = (float)((C * cs - S * sn) * inv_scale);
+    Pf[2] = (float)((S * cs + C * sn) * inv_scale);
+}
+
 /* ------------------------------------------------------------------ */
 /* Scoring                                                              */
 /* ------------------------------------------------------------------ */
@@ -100,6 +125,8 @@ struct ScoreArgs {
     const float *q;                       /* [L][H][3][fc]: qr, qi, max(0, qam - qma) */
     const float2 *table;                  /* [t_len][fc]: per pair float4 (C0, C1, S0, S1) */
     int64_t t_lo, t_len;
+    int32_t by_pos;                       /* table rows by position (post-RoPE keys), else by delta */
+    float qx_scale;                       /* norm-term scale (1 / rope scaling for post-RoPE keys) */
     float *raw;                           /* [units*G][raw_stride] */
     int64_t raw_stride;
     int32_t *status;
@@ -186,7 +213,7 @@ __global__ void __launch_bounds__(SCORE_THREADS) k_score_raw(const ScoreArgs a) 
             for (int t = 0; t < FPL; t++) {
                 qr[g][t] = b[t];
                 qi[g][t] = b[FC + t];
-                qx[g][t] = b[2 * FC + t];
+                qx[g][t] = b[2 * FC + t] * a.qx_scale;
             }
         }
         const uint8_t *kbase = a.k[l] + (int64_t)h * a.head_stride;
@@ -199,7 +226,7 @@ __global__ void __launch_bounds__(SCORE_THREADS) k_score_raw(const ScoreArgs a) 
             for (int g = 0; g < G; g++) v[g] = 0.f;
             if (valid) {
                 const int p = a.pos[a.pos_shared ? (int64_t)c : (int64_t)u * a.n_cells + c];
-                const int64_t di = (int64_t)a.cur_pos - p - a.t_lo;
+                const int64_t di = a.by_pos ? (int64_t)p - a.t_lo : (int64_t)a.cur_pos - p - a.t_lo;
                 if (di < 0 || di >= a.t_len) {
                     atomicOr(a.status, ST_POSITION);
                     valid = false;
@@ -276,6 +303,8 @@ struct TmaScoreArgs {
     const float *q;                       /* [L][H][3][fc] */
     const float4 *table;                  /* [t_len][fc/2] (C0, C1, S0, S1) */
     int64_t t_lo, t_len;
+    int32_t by_pos;                       /* table rows by position (post-RoPE keys), else by delta */
+    float qx_scale;                       /* norm-term scale (1 / rope scaling for post-RoPE keys) */
     float *raw;
     int64_t raw_stride;
     int32_t *status;
@@ -509,7 +538,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                             const float2 m = *reinterpret_cast<const float2 *>(src + g * 3 * FC + FC + 2 * q);
                             qr[g][i] = pk2(r.x * inv17, r.y * inv17);
                             qi[g][i] = pk2(m.x * inv17, m.y * inv17);
-                            qx[g][i] = *reinterpret_cast<const f2_t *>(src + g * 3 * FC + 2 * FC + 2 * q);
+                            const float2 x = *reinterpret_cast<const float2 *>(src + g * 3 * FC + 2 * FC + 2 * q);
+                            qx[g][i] = pk2(x.x * a.qx_scale, x.y * a.qx_scale);
                         }
                 }
                 const int hoff = h * a.row_bytes;
@@ -637,7 +667,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                 const int32_t *hp = rp + hh * SC_T;
                 const bool act = lane < cells;
                 const int p = act ? hp[lane] : 0;
-                const int64_t d = (int64_t)a.cur_pos - p - a.t_lo;
+                const int64_t d = a.by_pos ? (int64_t)p - a.t_lo : (int64_t)a.cur_pos - p - a.t_lo;
                 const bool ok = act && d >= 0 && d < a.t_len;
                 const int pprev = __shfl_up_sync(0xffffffffu, p, 1);
                 const bool okprev = __shfl_up_sync(0xffffffffu, ok ? 1 : 0, 1) != 0;
@@ -648,14 +678,14 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                 const unsigned startm = __ballot_sync(0xffffffffu, start);
                 const unsigned after = lane < 31 ? contm >> (lane + 1) : 0u;
                 const int len = start ? __ffs(~after) : 0;         /* this run's cells, from its first lane */
-                if (start) {
+                if (start) {                                 /* rows ascend with position or with delta */
                     mbar_expect(&full[st], (uint32_t)len * FC * 8);
-                    bulk_g2s(tab + (hh * SC_T + lane) * NQ, a.table + (d - len + 1) * NQ, (uint32_t)len * FC * 8,
-                             &full[st]);
+                    bulk_g2s(tab + (hh * SC_T + lane) * NQ, a.table + (a.by_pos ? d : d - len + 1) * NQ,
+                             (uint32_t)len * FC * 8, &full[st]);
                 }
                 const int s0 = max(0, 31 - __clz(startm & ((2u << lane) - 1u)));   /* first lane of my run */
                 const int rl = __shfl_sync(0xffffffffu, len, s0);
-                if (act) slot[hh * SC_T + lane] = ok ? hh * SC_T + 2 * s0 + rl - 1 - lane : -1;
+                if (act) slot[hh * SC_T + lane] = ok ? hh * SC_T + (a.by_pos ? lane : 2 * s0 + rl - 1 - lane) : -1;
                 if (lane == 0 && __popc(okm) != cells) atomicOr(a.status, ST_POSITION);
                 __syncwarp();
             }

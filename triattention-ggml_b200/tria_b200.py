@@ -63,7 +63,10 @@ class KvView(C.Structure):
                 ("n_head_kv", C.c_int32), ("head0", C.c_int32), ("n_cells", C.c_int32),
                 ("cell_stride", C.c_int64), ("head_stride", C.c_int64),
                 ("k", C.POINTER(C.c_void_p)), ("v", C.POINTER(C.c_void_p)),
-                ("pos", C.c_void_p), ("pos_shared", C.c_int32), ("reserved", C.c_int32)]
+                ("pos", C.c_void_p), ("pos_shared", C.c_int32), ("flags", C.c_int32)]
+
+
+VIEW_POST_ROPE = 1      # TRIA_VIEW_POST_ROPE
 
 
 class EvictParams(C.Structure):
@@ -247,7 +250,7 @@ def _stream(stream) -> int:
 
 
 def make_view(type_id, k_layers, v_layers, pos, n_cells, cell_stride, head_stride,
-              n_head_kv, layer0=0, head0=0, pos_shared=False):
+              n_head_kv, layer0=0, head0=0, pos_shared=False, flags=0):
     """Build a KvView; k_layers / v_layers are lists of torch tensors or device pointers.
     The returned view keeps its pointer arrays alive."""
     nl = len(k_layers)
@@ -256,7 +259,7 @@ def make_view(type_id, k_layers, v_layers, pos, n_cells, cell_stride, head_strid
     v = KvView(type_id, nl, layer0, n_head_kv, head0, n_cells, cell_stride, head_stride,
                C.cast(karr, C.POINTER(C.c_void_p)),
                C.cast(varr, C.POINTER(C.c_void_p)) if varr is not None else None,
-               _ptr(pos), 1 if pos_shared else 0, 0)
+               _ptr(pos), 1 if pos_shared else 0, int(flags))
     v._keep = (karr, varr, k_layers, v_layers, pos)
     return v
 
