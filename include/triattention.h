@@ -295,6 +295,35 @@ TRIA_API int tria_select_noalloc(const float *scores, int64_t score_stride,
                                  int32_t *kept_idx, int64_t kept_stride, int32_t *n_kept,
                                  void *stream);
 
+/* ---- Runtime policy of the reference's llama.cpp integration ----
+ * QUICKSTART.md:41-45: --tri-budget N (retention %), --tri-window N (recent
+ * tokens always kept), --tri-interval N (evict every N decoded tokens),
+ * --tri-sink N (first tokens always kept); the ramp stages 10/20/40/80/100 %
+ * of triattention.h's runtime.  New: the schedule as plain C so a bridge
+ * needs no logic of its own. */
+struct tria_policy {
+    int32_t budget_pct;     /* rows kept, % of the cache at the eviction (1..100) */
+    int32_t window;
+    int32_t interval;
+    int32_t sink;
+    int32_t step;           /* evictions so far (ramp stage) */
+    int32_t next_pos;       /* decode position of the next eviction */
+};
+TRIA_API void tria_policy_init(struct tria_policy *p, int32_t budget_pct, int32_t window,
+                               int32_t interval, int32_t sink);
+/* Whether an eviction is due at decode position n_past with n_kv rows cached
+ * (the first once n_kv exceeds window + sink + interval, then every interval
+ * positions); when due, fills *out (budget = budget_pct % of n_kv, at least 1;
+ * ramp stage of this step; window, sink) and advances the schedule. */
+TRIA_API int tria_policy_due(struct tria_policy *p, int32_t n_past, int32_t n_kv,
+                             struct tria_evict_params *out);
+/* Per-sequence cache length after an eviction: the maximum of the kept counts
+ * over each sequence's units.  n_kept [units] host counts (tria_get_n_kv),
+ * seq_of_unit [units] sequence index of each unit, n_seq sequences; writes
+ * n_kv [n_seq].  README.md:92's max-over-sequences, per sequence instead. */
+TRIA_API int tria_n_kv_per_seq(const int32_t *n_kept, const int32_t *seq_of_unit, int32_t units,
+                               int32_t n_seq, int32_t *n_kv);
+
 /* ---- Global budget across units (multi-sequence serving) ----
  * New; the reference has no counterpart.  A sequence keeps its best K rows
  * over all of its (layer, kv-head) units rather than a fixed count per unit:

@@ -109,3 +109,58 @@ TRIA_API void tria_free(struct tria_stats *s) {
     free(s->omega);
     free(s);
 }
+
+/* ---- runtime policy (host only) ---- */
+
+TRIA_API void tria_policy_init(struct tria_policy *p, int32_t budget_pct, int32_t window, int32_t interval,
+                               int32_t sink) {
+    if (!p) return;
+    memset(p, 0, sizeof *p);
+    p->budget_pct = budget_pct < 1 ? 1 : (budget_pct > 100 ? 100 : budget_pct);
+    p->window = window < 0 ? 0 : window;
+    p->interval = interval < 1 ? 1 : interval;
+    p->sink = sink < 0 ? 0 : sink;
+    p->next_pos = -1;
+}
+
+TRIA_API int tria_policy_due(struct tria_policy *p, int32_t n_past, int32_t n_kv, struct tria_evict_params *out) {
+    static const int32_t ramp[5] = {10, 20, 40, 80, 100};
+    if (!p || !out || n_past < 0 || n_kv < 0) {
+        tria_set_error("tria_policy_due: null argument or negative position");
+        return TRIA_ERR_INVALID;
+    }
+    if (p->next_pos < 0) {
+        /* first eviction: once the cache holds more than the protected rows plus one interval */
+        if ((int64_t)n_kv <= (int64_t)p->window + p->sink + p->interval) return 0;
+        p->next_pos = n_past;
+    }
+    if (n_past < p->next_pos) return 0;
+    int64_t b = (int64_t)n_kv * p->budget_pct / 100;
+    out->cur_pos = n_past;
+    out->budget = (int32_t)(b < 1 ? 1 : b);
+    out->ramp_pct = ramp[p->step < 4 ? p->step : 4];
+    out->window = p->window;
+    out->sink = p->sink;
+    out->reserved = 0;
+    p->step++;
+    p->next_pos = n_past + p->interval;
+    return 1;
+}
+
+TRIA_API int tria_n_kv_per_seq(const int32_t *n_kept, const int32_t *seq_of_unit, int32_t units, int32_t n_seq,
+                               int32_t *n_kv) {
+    if (!n_kept || !seq_of_unit || !n_kv || units < 0 || n_seq < 0) {
+        tria_set_error("tria_n_kv_per_seq: null argument or negative size");
+        return TRIA_ERR_INVALID;
+    }
+    for (int32_t s = 0; s < n_seq; s++) n_kv[s] = 0;
+    for (int32_t u = 0; u < units; u++) {
+        const int32_t s = seq_of_unit[u];
+        if (s < 0 || s >= n_seq) {
+            tria_set_error("tria_n_kv_per_seq: seq_of_unit[%d] = %d outside [0, %d)", u, s, n_seq);
+            return TRIA_ERR_INVALID;
+        }
+        if (n_kept[u] > n_kv[s]) n_kv[s] = n_kept[u];
+    }
+    return TRIA_OK;
+}

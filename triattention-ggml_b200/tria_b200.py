@@ -75,6 +75,33 @@ class EvictParams(C.Structure):
                 ("window", C.c_int32), ("sink", C.c_int32), ("reserved", C.c_int32)]
 
 
+class Policy(C.Structure):
+    """struct tria_policy: the reference runtime's eviction schedule."""
+    _fields_ = [("budget_pct", C.c_int32), ("window", C.c_int32), ("interval", C.c_int32),
+                ("sink", C.c_int32), ("step", C.c_int32), ("next_pos", C.c_int32)]
+
+    def __init__(self, budget_pct=75, window=512, interval=128, sink=0):
+        super().__init__()
+        lib().tria_policy_init(C.byref(self), int(budget_pct), int(window), int(interval), int(sink))
+
+    def due(self, n_past: int, n_kv: int):
+        """EvictParams when an eviction is due at n_past with n_kv cached rows, else None."""
+        out = EvictParams()
+        r = lib().tria_policy_due(C.byref(self), int(n_past), int(n_kv), C.byref(out))
+        if r < 0:
+            check(r)
+        return out if r == 1 else None
+
+
+def n_kv_per_seq(n_kept, seq_of_unit, n_seq):
+    """tria_n_kv_per_seq: per-sequence maximum of the kept counts."""
+    nk = np.ascontiguousarray(n_kept, np.int32)
+    so = np.ascontiguousarray(seq_of_unit, np.int32)
+    out = np.zeros(n_seq, np.int32)
+    check(lib().tria_n_kv_per_seq(nk.ctypes.data, so.ctypes.data, int(nk.shape[0]), int(n_seq), out.ctypes.data))
+    return out
+
+
 def build() -> str:
     """Compile the library in-tree (nvcc, sm_100a)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
@@ -118,6 +145,10 @@ def lib() -> C.CDLL:
                                           C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
                                           C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]
         L.tria_znorm_stats.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]
+        L.tria_policy_init.restype = None
+        L.tria_policy_init.argtypes = [C.POINTER(Policy), C.c_int32, C.c_int32, C.c_int32, C.c_int32]
+        L.tria_policy_due.argtypes = [C.POINTER(Policy), C.c_int32, C.c_int32, C.POINTER(EvictParams)]
+        L.tria_n_kv_per_seq.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]
         L.tria_score_key.restype = C.c_uint32
         L.tria_score_key.argtypes = [C.c_float]
         L.tria_key_histogram.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int32, C.c_int32, C.c_uint32,
