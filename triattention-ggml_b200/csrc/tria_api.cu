@@ -414,21 +414,6 @@ static void fill_score_args(const tria_ctx *c, const tria_kv_view *v, const int3
     }
 }
 
-/* k_znorm_walk over `chains` chains; its ring needs opt-in dynamic shared memory. */
-static cudaError_t znorm_walk_launch(const ZArgs &z, int chains, cudaStream_t st) {
-    static thread_local int configured_device = -1;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (configured_device != dev) {
-        e = cudaFuncSetAttribute(k_znorm_walk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(ZwShared));
-        if (e != cudaSuccess) return e;
-        configured_device = dev;
-    }
-    k_znorm_walk<<<(chains + ZW_WARPS - 1) / ZW_WARPS, ZW_WARPS * 32, sizeof(ZwShared), st>>>(z);
-    return cudaGetLastError();
-}
-
 static int launch_znorm(tria_ctx *c, int64_t unit0, int units, const int32_t *n_rows, cudaStream_t st) {
     ZArgs z;
     z.raw = c->raw + unit0 * c->G * c->raw_stride;
@@ -436,10 +421,10 @@ static int launch_znorm(tria_ctx *c, int64_t unit0, int units, const int32_t *n_
     z.G = (int32_t)c->G;
     z.units = units;
     z.ms = c->ms + unit0 * c->G;
-    z.status = c->d_status;
     for (int u = 0; u < units; u++) z.n_rows[u] = n_rows[unit0 + u];
     const int chains = units * (int)c->G;
-    CUDA_TRY(znorm_walk_launch(z, chains, st));
+    if (chains > 0) k_znorm_seg<<<chains, ZS_WARPS * 32, 0, st>>>(z);
+    CUDA_TRY(cudaGetLastError());
     c->launches++;
     return TRIA_OK;
 }
@@ -887,9 +872,9 @@ extern "C" TRIA_API int tria_znorm_stats(const float *x, int64_t stride, const i
         z.G = 1;
         z.units = cn;
         z.ms = reinterpret_cast<float2 *>(mean_std) + c0;
-        z.status = nullptr;
         for (int i = 0; i < cn; i++) z.n_rows[i] = n[c0 + i];
-        CUDA_TRY(znorm_walk_launch(z, cn, (cudaStream_t)stream));
+        if (cn > 0) k_znorm_seg<<<cn, ZS_WARPS * 32, 0, (cudaStream_t)stream>>>(z);
+        CUDA_TRY(cudaGetLastError());
     }
     return TRIA_OK;
 }

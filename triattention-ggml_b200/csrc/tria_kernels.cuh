@@ -18,14 +18,15 @@
  *                     raw_g = (sum_f qr_gf X_f + qi_gf Y_f) / 17 + sum_f res_gf |k_f|
  *                  which is triattention.c:156-192 with the offset sum moved
  *                  into the table (rel_r cos - rel_i sin summed over o).
- *   k_znorm_walk   mean and variance bit-identical to the reference's
- *                  sequential fp32 chains (triattention.c:228-236), a warp
- *                  advancing a chain 512 elements per step as ulp-grid
- *                  translations; IEEE div/sqrt, std clamp 1e-6.
+ *   k_znorm_seg    mean and variance bit-identical to the reference's
+ *                  sequential fp32 chains (triattention.c:228-236): segments
+ *                  of 128 elements precomputed as ulp-grid translations, then
+ *                  walked 32 segments per step; IEEE div/sqrt, std clamp 1e-6.
  *   k_select       z-score max over the group (triattention.c:240-247), an
- *                  order-preserving 32-bit key, 8-bit radix select of the
- *                  keep-th largest key, ties to the lowest rows, and an
- *                  ordered block scan that writes kept row indices in order.
+ *                  order-preserving 32-bit key, radix select (12-, 10- and
+ *                  10-bit digits) of the keep-th largest key, ties to the
+ *                  lowest rows, and warp ballots over contiguous row ranges
+ *                  that write the kept row indices in order.
  *   k_compact      stable gather of kept K/V rows and positions into the
  *                  ping-pong buffer, vectorised, byte-exact.
  *
@@ -286,6 +287,7 @@ constexpr int WS_THREADS = (WS_CWARPS + 4) * 32;   /* + a producer warpgroup, on
  * most the launch total, or the increase would wait forever; the host checks
  * the compiled register count before every launch. */
 constexpr int WS_LAUNCH_REGS = 168;
+constexpr int WS_PREFETCH = 2;          /* items whose K tiles are prefetched to L2 beyond the stages */
 constexpr int WS_PRODUCER_REGS = 72;
 constexpr int WS_CONSUMER_REGS = 216;
 constexpr int WS_RWARPS = 3;           /* reducer warps: the producer warpgroup's other three */
@@ -352,6 +354,10 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+/* Bulk prefetch global -> L2 (no shared memory, no completion to wait for). */
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
@@ -634,11 +640,22 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                 bulk_g2s(ring + (kk % WS_POS_RING) * plan.pos_ints + lane * SC_T, src, pb, bar);
             }
         };
+        /* K tile of item kk -> L2 ahead of its copy: the copy into a stage can only
+         * start when the consumers release that stage, so with few stages a copy
+         * straight from DRAM would leave them waiting for its latency */
+        auto prefetch_k = [&](int kk) {
+            if (lane != 0 || kk >= n_mine) return;
+            int l, c0;
+            const int cells = item_of(kk, l, c0);
+            if (cells > 0) bulk_prefetch_l2(a.k[l] + (int64_t)c0 * a.cell_stride, (uint32_t)(cells * a.cell_stride));
+        };
         int pos_issued = 0;                              /* items whose positions were requested */
         for (; pos_issued < min(WS_POS_RING - 1, n_mine); pos_issued++) fetch_pos(pos_issued);
+        for (int kk = S; kk < S + WS_PREFETCH - 1; kk++) prefetch_k(kk);
         int k = 0;
         for (; k < n_mine && !s_abort; k++) {
             const int st = k % S;
+            prefetch_k(k + S + WS_PREFETCH - 1);
             if (pos_issued < n_mine) fetch_pos(pos_issued++);   /* ring slot of item k-1: done with */
             if (!mbar_wait(&posbar[k % WS_POS_RING], (uint32_t)((k / WS_POS_RING) & 1)) ||
                 !mbar_wait(&empty[st], (uint32_t)(((k / S) & 1) ^ 1))) {
@@ -764,305 +781,281 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
 /*
  * triattention.c:228-236 forms mean = fl(sum)/n and var with two sequential
  * fp32 chains  s <- fl(s + v_k).  Summing more accurately would move z by up
- * to ~1e-5 at 32k rows, so the chains are reproduced bit for bit, but a warp
- * advances them 512 elements per step:
+ * to ~1e-5 at 32k rows, so the chains are reproduced bit for bit, in parallel:
  *
  * While s and every partial result stay in one binade [2^E, 2^(E+1)), each
  * fp32 add rounds on the fixed grid ulp = 2^(E-23): with s = M*ulp (M the
  * signed 24-bit significand), fl(s + v) = (M + round(v/ulp))*ulp, ties to
- * even M.  A step takes E and M from the running s, lets every lane turn its
- * 16 consecutive elements into integer increments, forms their in-order
- * prefix sums (lane prefix + warp scan; ties resolved in order by parity),
- * and accepts the longest prefix whose partial significands stay strictly
- * inside (2^23, 2^24) -- which proves every exact s_k + v_k lay inside the
- * binade, so the grid rounding was the fp32 rounding.  The first element that
- * leaves the binade (or is not finite) is added with one plain fp32 add and
- * the walk resumes after it.  The common step (no tie, no exit) is decided
- * from each lane's prefix extremes and one vote.  When a block needs more
- * than ZW_WALK_STEPS steps -- s is small next to its elements, as near the
- * start of a chain or where a zero-mean sum wanders near 0 -- one lane adds
- * the rest of the block with plain fp32 adds from shared memory (4 cycles an
- * element), which beats a 512-wide step per binade exit.  The result equals
- * the reference's chain for every input.  One warp walks one chain; its data
- * streams through a per-warp ring of bulk copies.  Waits are bounded
- * (ST_TIMEOUT).
+ * even M.  v*2^(23-E) + 1.5*2^23 rounds v/ulp to an integer with one fp32
+ * add (no conversion), so a run of elements becomes integer increments whose
+ * prefix sums are the partial significands; when every one of them stays
+ * inside [2^23 + 1, 2^24 - 1] each exact s_k + v_k lay inside the binade and
+ * the grid rounding was the fp32 rounding.
+ *
+ * k_znorm_seg runs one CTA per chain, two passes (sum, then sum of squared
+ * deviations from the fp32 mean), each over windows of ZS_WIN segments of
+ * ZS_SEG elements:
+ *  - every warp turns its segments into records: with a binade E guessed
+ *    from an approximate prefix sum (the exact sum at the window start plus
+ *    the window's segment sums), the segment's elements become increments on
+ *    the grid of E, and the record keeps their total, the extremes of their
+ *    prefix sums, the number of ties (at most two) and the parity of each
+ *    tie's lower candidate;
+ *  - warp 0 then advances the exact fp32 sum: all the window's records at
+ *    once when they carry the binade the sum is in and every partial
+ *    significand stays inside the binade (a warp scan of the totals gives
+ *    each record's start), a record with ties on its own (each tie rounds to
+ *    the even candidate), and anything else -- a crossing of the binade, a
+ *    zero or subnormal sum, an element too large for the grid, NaN or Inf --
+ *    as the reference's plain fp32 adds, one element after the other.
+ * The result is the reference's sequential chain bit for bit.  While warp 0
+ * walks a window the other warps already load the next one; the plain adds
+ * read the window's values from shared memory.
  */
-
-constexpr int ZW_WARPS = 4;                      /* chains per CTA */
-constexpr int ZW_EPL = 16;                       /* elements per lane per step */
-constexpr int ZW_BLOCK = 32 * ZW_EPL;            /* 512 elements per step / ring slot */
-constexpr int ZW_STAGES = 8;                     /* 16 KB of copies in flight per chain */
-constexpr int ZW_WALK_STEPS = 2;                 /* walk steps per block before plain adds */
-
 struct ZArgs {
     const float *raw;
     int64_t raw_stride;                  /* floats, multiple of 4 */
     int32_t G, units;
     float2 *ms;                          /* [units*G] (mean, std) */
-    int32_t *status;                     /* may be NULL */
     int32_t n_rows[TRIA_MAX_UNITS];
 };
 
-/* v[idx] of register array v with a runtime idx, without spilling v. */
-template <int N>
-__device__ __forceinline__ float pick(const float (&v)[N], int idx) {
-    float r = v[0];
+constexpr int ZS_SEG = 128;                        /* elements per segment: 4 per lane */
+constexpr int ZS_WARPS = 4;
+constexpr int ZS_WIN = 32;                         /* segments per window: one walk batch */
+constexpr int ZS_SPW = ZS_WIN / ZS_WARPS;          /* segments per warp per window */
+constexpr uint32_t ZS_SLOW = 1u << 13;             /* record flag: walk the segment element by element */
+
+struct ZsRec {
+    uint32_t f;                                    /* biased exponent | ties << 9 | parities << 11 | ZS_SLOW */
+    int32_t delta, pmin, pmax;                     /* total increment, extremes of the prefix sums */
+};
+
+/* x has the sign sg and a magnitude in [2^23 + 1, 2^24 - 1] */
+__device__ __forceinline__ bool zs_ok(int x, int sg) {
+    return (uint32_t)(x * sg) - ((1u << 23) + 1u) <= (1u << 23) - 2u;
+}
+
+/* The record of one segment whose lane elements are xs[0..3] (dead ones 0),
+ * under the binade of `approx`; the result is the same in every lane. */
+__device__ __forceinline__ ZsRec zs_record(const float (&xs)[4], double approx) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t ab = __float_as_uint((float)approx);
+    const int exb = (ab >> 23) & 0xff;
+    bool slow = exb == 0 || exb == 255 || exb < 23;              /* E = exb - 127 >= -104: 2^(23-E) is a float */
+    const float scale = slow ? 1.f : __int_as_float((150 - (exb - 127)) << 23);
+    int lsum = 0, pl = 0x7fffffff, ph = -0x7fffffff - 1, tc = 0, tp1 = 0, tp2 = 0;
+    bool out = false;
 #pragma unroll
-    for (int t = 1; t < N; t++) r = t == idx ? v[t] : r;
+    for (int t = 0; t < 4; t++) {
+        const float q = xs[t] * scale;
+        const bool o = !(fabsf(q) < 0x1p22f);
+        const float f = __fadd_rn(q, 0x1.8p23f);
+        const float fr = __fsub_rn(q, __fsub_rn(f, 0x1.8p23f));
+        const bool tie = !o && fabsf(fr) == 0.5f;
+        int dd = (int)((uint32_t)__float_as_int(f) - 0x4b400000u) - ((tie && fr < 0.f) ? 1 : 0);
+        dd = o ? 0 : dd;
+        out |= o;
+        lsum += dd;
+        pl = min(pl, lsum);
+        ph = max(ph, lsum);
+        if (tie) {
+            if (tc == 0) tp1 = lsum; else if (tc == 1) tp2 = lsum;
+            tc++;
+        }
+    }
+    int incl = lsum;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, m);
+        if (lane >= m) incl += y;
+    }
+    const int ex = incl - lsum;
+    ZsRec r;
+    r.delta = __shfl_sync(0xffffffffu, incl, 31);
+    r.pmin = __reduce_min_sync(0xffffffffu, ex + pl);
+    r.pmax = __reduce_max_sync(0xffffffffu, ex + ph);
+    const int nt = (int)__reduce_add_sync(0xffffffffu, (unsigned)tc);
+    slow |= __any_sync(0xffffffffu, out) || nt > 2;
+    /* parities of the ties' lower candidates (relative prefix sums), in element order */
+    const unsigned tm = __ballot_sync(0xffffffffu, tc > 0);
+    uint32_t par = 0;
+    if (tm) {
+        const int A = __ffs(tm) - 1;
+        par = (uint32_t)__shfl_sync(0xffffffffu, ex + tp1, A) & 1u;
+        const int tcA = __shfl_sync(0xffffffffu, tc, A);
+        const unsigned rest = tm & ~(1u << A);
+        const int B = rest ? __ffs(rest) - 1 : A;
+        const int p2a = __shfl_sync(0xffffffffu, ex + tp2, A);
+        const int p2b = __shfl_sync(0xffffffffu, ex + tp1, B);
+        if (nt >= 2) par |= ((uint32_t)(tcA >= 2 ? p2a : p2b) & 1u) << 1;
+    }
+    r.f = (uint32_t)exb | ((uint32_t)min(nt, 3) << 9) | (par << 11) | (slow ? ZS_SLOW : 0u);
     return r;
 }
 
-struct ZwShared {
-    float ring[ZW_WARPS][ZW_STAGES][ZW_BLOCK];
-    uint64_t bar[ZW_WARPS][ZW_STAGES];
-};
-
-/* One warp: the fp32 sequential sum of val(x[0..n)), reading ring blocks
- * [blk0, blk0 + nb) of its stream (block b of the stream = data block
- * b % nb).  `issue(b)` requests stream block b.  Returns the sum (all lanes). */
-template <class Val, class Issue>
-__device__ float walk_chain(const float *ring_base, uint64_t *bars, int n, int nb, int blk0, int total_blocks,
-                            Val val, Issue issue, int32_t *status, bool &aborted) {
+/* The reference's plain fp32 adds of v[0..cnt) onto s, v already val()'d
+ * and staged in shared memory (lane 0; all lanes get the sum). */
+__device__ __forceinline__ float zs_serial(const float *v, int cnt, float s) {
     const int lane = threadIdx.x & 31;
-    float s = 0.f;
-    for (int bi = 0; bi < nb; bi++) {
-        const int g = blk0 + bi;                        /* stream block */
-        const int st = g % ZW_STAGES;
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars[st], (uint32_t)((g / ZW_STAGES) & 1)))) {
-            if (lane == 0 && status) atomicOr(status, ST_TIMEOUT);
-            aborted = true;
-            return __int_as_float(0x7fc00000);          /* NaN: the status says why */
-        }
-        const float *blk = ring_base + st * ZW_BLOCK;
-        const int base = bi * ZW_BLOCK;
-        const int cnt = min(ZW_BLOCK, n - base);
-        float v[ZW_EPL];
+    float acc = s;
+    if (lane == 0) {
+        int e = 0;
+        for (; e + 16 <= cnt; e += 16) {
+            float4 w[4];
 #pragma unroll
-        for (int t = 0; t < ZW_EPL; t += 4) {
-            const float4 w = *reinterpret_cast<const float4 *>(blk + lane * ZW_EPL + t);
-            v[t] = val(w.x); v[t + 1] = val(w.y); v[t + 2] = val(w.z); v[t + 3] = val(w.w);
+            for (int i = 0; i < 4; i++) w[i] = *reinterpret_cast<const float4 *>(v + e + 4 * i);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                acc = __fadd_rn(acc, w[i].x);
+                acc = __fadd_rn(acc, w[i].y);
+                acc = __fadd_rn(acc, w[i].z);
+                acc = __fadd_rn(acc, w[i].w);
+            }
         }
-        int p = 0;                                      /* first element of the block not yet added */
-        int steps = 0;
-        while (p < cnt) {
-            if (++steps > ZW_WALK_STEPS) {
-                /* s keeps leaving its binade (it is small next to the elements): the
-                 * rest of the block as plain fp32 adds by one lane, from shared memory */
-                float acc = s;
-                if (lane == 0) {
-                    int e = p;
-                    for (; e < cnt && (e & 3); e++) acc = __fadd_rn(acc, val(blk[e]));
-                    for (; e + 4 <= cnt; e += 4) {
-                        const float4 w = *reinterpret_cast<const float4 *>(blk + e);
-                        acc = __fadd_rn(acc, val(w.x));
-                        acc = __fadd_rn(acc, val(w.y));
-                        acc = __fadd_rn(acc, val(w.z));
-                        acc = __fadd_rn(acc, val(w.w));
-                    }
-                    for (; e < cnt; e++) acc = __fadd_rn(acc, val(blk[e]));
-                }
-                s = __shfl_sync(0xffffffffu, acc, 0);
-                break;
-            }
-            const uint32_t bits = __float_as_uint(s);
-            const int exb = (bits >> 23) & 0xff;
-            if (exb == 0 || exb == 255) {               /* s zero / subnormal / not finite: one plain add */
-                s = __fadd_rn(s, __shfl_sync(0xffffffffu, pick(v, p % ZW_EPL), p / ZW_EPL));
-                p++;
-                continue;
-            }
-            const int E = exb - 127;
-            if (E < -104) {                             /* s so small that 2^(23-E) is not a float */
-                s = __fadd_rn(s, __shfl_sync(0xffffffffu, pick(v, p % ZW_EPL), p / ZW_EPL));
-                p++;
-                continue;
-            }
+        for (; e < cnt; e++) acc = __fadd_rn(acc, v[e]);
+    }
+    return __shfl_sync(0xffffffffu, acc, 0);
+}
+
+/* Warp 0: advance s over the window's records s_rec[0..cnt) (<= 32); the
+ * window's values are staged in s_vals (ZS_SEG per segment), `n_last` of
+ * them live in the last segment. */
+__device__ __forceinline__ float zs_walk(const ZsRec *s_rec, int cnt, const float *s_vals, int n_last, float s) {
+    const int lane = threadIdx.x & 31;
+    ZsRec r = lane < cnt ? s_rec[lane] : ZsRec{ZS_SLOW, 0, 0, 0};
+    int cur = 0;
+    while (cur < cnt) {
+        uint32_t bits = __float_as_uint(s);
+        const int exb = (bits >> 23) & 0xff;
+        const bool normal = exb != 0 && exb != 255 && exb >= 23;
+        int M = 0, sg = 1;
+        if (normal) {
             const int mabs = (int)((bits & 0x7fffffu) | 0x800000u);
-            const int M = (bits >> 31) ? -mabs : mabs;
-            /* live elements of this lane: [p, cnt) within [16*lane, 16*lane+16) */
-            const int lo = max(0, p - lane * ZW_EPL), hi = min(ZW_EPL, cnt - lane * ZW_EPL);
-            /* Increments: q = v * 2^(23-E) = v/ulp exactly.  For |q| < 2^22, f = q + 1.5*2^23
-             * lies in (2^23, 2^24) where the fp32 grid is the integers, so f rounds q to
-             * the nearest integer (ties to even) and bits(f) - bits(1.5*2^23) is that
-             * integer.  A tie (|q - r| == 1/2) takes the lower candidate and is settled
-             * by parity below.  |q| >= 2^22 (or not finite) marks the element "out":
-             * it is added with a plain fp32 add.  Dead elements count as 0. */
-            const float scale = __int_as_float((150 - E) << 23);
-            /* increments and their sums are kept modulo 2^32: every value that is used
-             * (partials inside the binade) is < 2^24 in magnitude, so wrap-around of
-             * discarded ones does no harm */
-            uint32_t d[ZW_EPL];
-            bool any_tie = false, any_out = false;
-            uint32_t lsum = 0;
-            int pmin = 0x7fffffff, pmax = -0x7fffffff - 1;   /* extremes of this lane's prefix sums */
-#pragma unroll
-            for (int t = 0; t < ZW_EPL; t++) {
-                const float x = (t >= lo && t < hi) ? v[t] : 0.f;
-                const float q = x * scale;
-                const bool out = !(fabsf(q) < 0x1p22f);
-                const float f = __fadd_rn(q, 0x1.8p23f);
-                const float fr = __fsub_rn(q, __fsub_rn(f, 0x1.8p23f));
-                const bool ist = fabsf(fr) == 0.5f;
-                uint32_t dd = (uint32_t)(__float_as_int(f) - 0x4b400000) - ((ist && fr < 0.f) ? 1u : 0u);
-                dd = out ? 0u : dd;
-                any_tie |= ist && !out;
-                any_out |= out;
-                d[t] = dd;
-                lsum += dd;
-                /* |increment| <= 2^22, so a lane's prefix sums fit an int */
-                pmin = min(pmin, (int)lsum);
-                pmax = max(pmax, (int)lsum);
-            }
-            /* exclusive warp scan of the lane totals */
-            uint32_t inc = lsum;
+            M = (bits >> 31) ? -mabs : mabs;
+            sg = M > 0 ? 1 : -1;
+            /* whole records from cur on: plain ones in this binade */
+            const bool mine = lane >= cur && lane < cnt;
+            const int dl = mine ? r.delta : 0;
+            int incl = dl;
 #pragma unroll
             for (int m = 1; m < 32; m <<= 1) {
-                const uint32_t y = __shfl_up_sync(0xffffffffu, inc, m);
-                if (lane >= m) inc += y;
+                const int y = __shfl_up_sync(0xffffffffu, incl, m);
+                if (lane >= m) incl += y;
             }
-            uint32_t off = inc - lsum;                       /* sum of increments of earlier lanes */
-            /* Whole step at once when no element is a tie or out and both extremes of
-             * every lane's partial significands (dead elements repeat the partial before
-             * them) lie inside [2^23 + 1, 2^24 - 1] -- then all of them do.  A lane whose
-             * earlier lanes all pass has an exact `off`; the first failing lane therefore
-             * sees true values and fails, so wrap-around cannot pass a bad step. */
-            {
-                const uint32_t sg = M > 0 ? 1u : 0xffffffffu;
-                const uint32_t b0 = (uint32_t)M + off;
-                const bool in_lo = ((b0 + (uint32_t)pmin) * sg - ((1u << 23) + 1u)) <= (1u << 23) - 2u;
-                const bool in_hi = ((b0 + (uint32_t)pmax) * sg - ((1u << 23) + 1u)) <= (1u << 23) - 2u;
-                const bool ok = !any_tie && !any_out && in_lo && in_hi;
-                if (__all_sync(0xffffffffu, ok)) {
-                    const uint32_t part = __shfl_sync(0xffffffffu, (uint32_t)M + inc, 31);
-                    const uint32_t a = M > 0 ? part : 0u - part;
-                    s = __uint_as_float((bits & 0x80000000u) | ((uint32_t)exb << 23) | (a & 0x7fffffu));
-                    p = cnt;
-                    continue;
-                }
-            }
-            /* slow step: per-element tie / out / live masks */
-            const unsigned live = hi > lo ? (((hi >= 32 ? 0u : (1u << hi)) - 1u) & ~((1u << lo) - 1u)) : 0u;
-            unsigned tie = 0, bad = 0;
-#pragma unroll
-            for (int t = 0; t < ZW_EPL; t++) {
-                const float x = (t >= lo && t < hi) ? v[t] : 0.f;
-                const float q = x * scale;
-                const bool out = !(fabsf(q) < 0x1p22f);
-                const float fr = __fsub_rn(q, __fsub_rn(__fadd_rn(q, 0x1.8p23f), 0x1.8p23f));
-                tie |= (!out && fabsf(fr) == 0.5f ? 1u : 0u) << t;
-                bad |= (out ? 1u : 0u) << t;
-            }
-            /* ties in element order: the candidate with an even significand */
-            unsigned tmask = __ballot_sync(0xffffffffu, tie != 0);
-            while (tmask) {
-                const int tl = __ffs(tmask) - 1;
-                uint32_t adj = 0;
-                int tt = 0;
-                if (lane == tl) {
-                    tt = __ffs(tie) - 1;
-                    uint32_t upto = off;                     /* increments up to and including tt */
-#pragma unroll
-                    for (int t = 0; t < ZW_EPL; t++) if (t <= tt) upto += d[t];
-                    /* candidates M+upto (lower) and M+upto+1: keep the even one */
-                    adj = ((uint32_t)M + upto) & 1u;
-                    tie &= ~(1u << tt);
-                }
-                adj = __shfl_sync(0xffffffffu, adj, tl);
-                tt = __shfl_sync(0xffffffffu, tt, tl);
-                if (lane == tl) {
-#pragma unroll
-                    for (int t = 0; t < ZW_EPL; t++) if (t == tt) d[t] += adj;
-                } else if (lane > tl) {
-                    off += adj;
-                }
-                tmask = __ballot_sync(0xffffffffu, tie != 0);
-            }
-            /* first element whose partial significand leaves the open binade */
-            int first_bad = ZW_BLOCK;
-            {
-                /* |run| must stay in [2^23 + 1, 2^24 - 1]; work on the magnitude */
-                const uint32_t sg = M > 0 ? 1u : 0xffffffffu;
-                uint32_t run = ((uint32_t)M + off) * sg;
-                unsigned outm = bad;
-#pragma unroll
-                for (int t = 0; t < ZW_EPL; t++) {
-                    run += d[t] * sg;
-                    outm |= (run - ((1u << 23) + 1u) > (1u << 23) - 2u ? 1u : 0u) << t;
-                }
-                outm &= live;
-                if (outm) first_bad = lane * ZW_EPL + __ffs(outm) - 1;
-            }
-#pragma unroll
-            for (int m = 16; m; m >>= 1) first_bad = min(first_bad, __shfl_xor_sync(0xffffffffu, first_bad, m));
-            const int stop = min(first_bad, cnt);       /* elements [p, stop) are exact translations */
-            if (stop > p) {
-                /* M + (increments of elements < stop): from the lane that holds element stop-1 */
-                const int hl = (stop - 1) / ZW_EPL, ht = (stop - 1) % ZW_EPL;
-                uint32_t part = (uint32_t)M + off;
-#pragma unroll
-                for (int t = 0; t < ZW_EPL; t++) if (t <= ht) part += d[t];
-                part = __shfl_sync(0xffffffffu, part, hl);
-                const uint32_t a = M > 0 ? part : 0u - part;
-                s = __uint_as_float((bits & 0x80000000u) | ((uint32_t)exb << 23) | (a & 0x7fffffu));
-            }
-            p = stop;
-            if (p < cnt) {                              /* the element that left the binade */
-                s = __fadd_rn(s, __shfl_sync(0xffffffffu, pick(v, p % ZW_EPL), p / ZW_EPL));
-                p++;
+            const int ex = incl - dl;
+            const bool ok = mine && (r.f & (0x1ffu | ZS_SLOW | (3u << 9))) == (uint32_t)exb &&
+                            zs_ok(M + ex + r.pmin, sg) && zs_ok(M + ex + r.pmax, sg);
+            const unsigned bad = __ballot_sync(0xffffffffu, mine && !ok);
+            const int stop = bad ? __ffs(bad) - 1 : cnt;
+            if (stop > cur) {
+                M += __shfl_sync(0xffffffffu, incl, stop - 1);
+                bits = (bits & 0x80000000u) | ((uint32_t)exb << 23) | ((uint32_t)(M * sg) & 0x7fffffu);
+                s = __uint_as_float(bits);
+                cur = stop;
+                if (cur >= cnt) break;
             }
         }
-        __syncwarp();
-        if (lane == 0 && g + ZW_STAGES < total_blocks) issue(g + ZW_STAGES);
+        /* record cur on its own: ties, or walked element by element */
+        const uint32_t f = __shfl_sync(0xffffffffu, r.f, cur);
+        const int delta = __shfl_sync(0xffffffffu, r.delta, cur);
+        const int pmin = __shfl_sync(0xffffffffu, r.pmin, cur);
+        const int pmax = __shfl_sync(0xffffffffu, r.pmax, cur);
+        const int nt = (int)((f >> 9) & 3u);
+        if (normal && (f & 0x1ffu) == (uint32_t)exb && !(f & ZS_SLOW) && nt <= 2 &&
+            zs_ok(M + pmin, sg) && zs_ok(M + pmax + nt, sg)) {
+            const int a1 = nt >= 1 ? ((M + (int)((f >> 11) & 1u)) & 1) : 0;
+            const int a2 = nt >= 2 ? ((M + (int)((f >> 12) & 1u) + a1) & 1) : 0;
+            const int m2 = M + delta + a1 + a2;
+            s = __uint_as_float((bits & 0x80000000u) | ((uint32_t)exb << 23) | ((uint32_t)(m2 * sg) & 0x7fffffu));
+        } else {
+            s = zs_serial(s_vals + cur * ZS_SEG, cur == cnt - 1 ? n_last : ZS_SEG, s);
+        }
+        cur++;
     }
     return s;
 }
 
-/* One warp per (unit, query head) chain: (mean, std) of triattention.c:227-238. */
-__global__ void __launch_bounds__(ZW_WARPS * 32, 1) k_znorm_walk(const ZArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    ZwShared &sh = *reinterpret_cast<ZwShared *>(smem);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * ZW_WARPS + warp;
-    const bool live = t < a.units * a.G;
-    if (lane == 0)
-        for (int i = 0; i < ZW_STAGES; i++) mbar_init(&sh.bar[warp][i], 1);
-    if (threadIdx.x == 0) asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+/* One pass of a chain: the sequential fp32 sum of val(x[0..n)).  All threads
+ * of the CTA call it; it returns the sum in every thread. */
+template <class Val>
+__device__ float zs_pass(const float *x, int n, Val val, float *s_sum, ZsRec *s_rec, float *s_vals, float *s_state) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nseg = (n + ZS_SEG - 1) / ZS_SEG;
+    if (tid == 0) *s_state = 0.f;
+    for (int w0 = 0; w0 < nseg; w0 += ZS_WIN) {
+        const int wcnt = min(ZS_WIN, nseg - w0);
+        /* this warp's segments warp, warp + ZS_WARPS, ... of the window: values and sums */
+        float xs[ZS_SPW][4];
+#pragma unroll
+        for (int j = 0; j < ZS_SPW; j++) {
+            const int sl = warp + ZS_WARPS * j;
+            const int e = (w0 + sl) * ZS_SEG + 4 * lane;
+            const int live = sl < wcnt ? max(0, min(4, n - e)) : 0;
+            float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (live > 0) w = *reinterpret_cast<const float4 *>(x + e);   /* e + 3 < stride: e % 4 == 0, e < n */
+            xs[j][0] = live > 0 ? val(w.x) : 0.f;
+            xs[j][1] = live > 1 ? val(w.y) : 0.f;
+            xs[j][2] = live > 2 ? val(w.z) : 0.f;
+            xs[j][3] = live > 3 ? val(w.w) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < ZS_SPW; j++) {
+            float t = (xs[j][0] + xs[j][1]) + (xs[j][2] + xs[j][3]);
+#pragma unroll
+            for (int m = 16; m; m >>= 1) t += __shfl_xor_sync(0xffffffffu, t, m);
+            const int sl = warp + ZS_WARPS * j;
+            if (lane == 0 && sl < wcnt) s_sum[sl] = t;
+        }
+        __syncthreads();        /* window sums; the exact sum at the window start; the walk of the last window is over */
+#pragma unroll
+        for (int j = 0; j < ZS_SPW; j++)                /* values for the walk's plain adds */
+            *reinterpret_cast<float4 *>(s_vals + (warp + ZS_WARPS * j) * ZS_SEG + 4 * lane) =
+                make_float4(xs[j][0], xs[j][1], xs[j][2], xs[j][3]);
+        /* approximate prefix sums at each segment start (one segment per lane) */
+        const double a0 = lane < wcnt ? (double)s_sum[lane] : 0.0;
+        double inc = a0;
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) {
+            const double y = __shfl_up_sync(0xffffffffu, inc, m);
+            if (lane >= m) inc += y;
+        }
+        const double pre = (double)*s_state + (inc - a0);
+#pragma unroll
+        for (int j = 0; j < ZS_SPW; j++) {
+            const int sl = warp + ZS_WARPS * j;
+            const ZsRec r = zs_record(xs[j], __shfl_sync(0xffffffffu, pre, sl));
+            if (lane == 0 && sl < wcnt) s_rec[sl] = r;
+        }
+        __syncthreads();                               /* the window's records and values */
+        if (warp == 0) {
+            const int n_last = min(ZS_SEG, n - (w0 + wcnt - 1) * ZS_SEG);
+            const float s = zs_walk(s_rec, wcnt, s_vals, n_last, *s_state);
+            if (lane == 0) *s_state = s;
+        }
+    }
     __syncthreads();
-    if (!live) return;
+    const float s = *s_state;
+    __syncthreads();                                   /* every thread has read it before the next reset */
+    return s;
+}
+
+/* One CTA per (unit, query head) chain: (mean, std) of triattention.c:227-238. */
+__global__ void __launch_bounds__(ZS_WARPS * 32, 8) k_znorm_seg(const ZArgs a) {
+    __shared__ float s_sum[ZS_WIN];
+    __shared__ ZsRec s_rec[ZS_WIN];
+    __shared__ __align__(16) float s_vals[ZS_WIN * ZS_SEG];
+    __shared__ float s_state;
+    const int t = blockIdx.x;
     const int n = a.n_rows[t / a.G];
     const float *x = a.raw + (int64_t)t * a.raw_stride;
-    const int nb = (n + ZW_BLOCK - 1) / ZW_BLOCK;
-    const int total = 2 * nb;                             /* the data twice: mean, then variance */
-    float *ring = &sh.ring[warp][0][0];
-    uint64_t *bars = sh.bar[warp];
-    int issued = 0;                                       /* lane 0's count of requested blocks */
-    auto issue = [&](int g) {                             /* lane 0: stream block g -> its slot */
-        const int b = g % nb;
-        const int st = g % ZW_STAGES;
-        const int cnt = min(ZW_BLOCK, n - b * ZW_BLOCK);
-        const uint32_t bytes = (uint32_t)((cnt + 3) / 4 * 16);   /* within the row: stride % 4 == 0 */
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive_tx(&bars[st], bytes);
-        bulk_g2s(ring + st * ZW_BLOCK, x + (int64_t)b * ZW_BLOCK, bytes, &bars[st]);
-        issued = g + 1;
-    };
-    if (lane == 0)
-        for (int g = 0; g < min(ZW_STAGES, total); g++) issue(g);
-    __syncwarp();
-    bool aborted = false;
-    const float sum = walk_chain(ring, bars, n, nb, 0, total, [](float v) { return v; }, issue, a.status, aborted);
+    const float sum = zs_pass(x, n, [](float v) { return v; }, s_sum, s_rec, s_vals, &s_state);
     const float mean = __fdiv_rn(sum, (float)n);
-    const float var = aborted ? sum : walk_chain(ring, bars, n, nb, nb, total, [mean](float v) {
+    const float var = zs_pass(x, n, [mean](float v) {
         const float d = __fsub_rn(v, mean);
         return __fmul_rn(d, d);
-    }, issue, a.status, aborted);
-    if (aborted) {                                        /* copies still in flight must land first */
-        if (lane == 0)
-            for (int g = max(0, issued - ZW_STAGES); g < issued; g++)
-                mbar_wait(&bars[g % ZW_STAGES], (uint32_t)((g / ZW_STAGES) & 1));
-        __syncwarp();
-    }
-    if (lane == 0) {
+    }, s_sum, s_rec, s_vals, &s_state);
+    if (threadIdx.x == 0) {
         float sd = __fsqrt_rn(__fdiv_rn(var, (float)n));
         if (sd < 1e-6f) sd = 1e-6f;
         a.ms[t] = make_float2(mean, sd);
@@ -1129,29 +1122,6 @@ struct SelectArgs {
     int32_t keep_req[TRIA_MAX_UNITS];
 };
 
-/* Exclusive block scan of one flag per thread; `total` = number of set flags. */
-__device__ __forceinline__ int block_excl_scan(bool f, int *s_warp, int &total) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const unsigned b = __ballot_sync(0xffffffffu, f);
-    const int pre = __popc(b & ((1u << lane) - 1u));
-    if (lane == 0) s_warp[w] = __popc(b);
-    __syncthreads();
-    if (w == 0) {
-        int v = lane < nw ? s_warp[lane] : 0;
-#pragma unroll
-        for (int m = 1; m < 32; m <<= 1) {
-            const int t = __shfl_up_sync(0xffffffffu, v, m);
-            if (lane >= m) v += t;
-        }
-        s_warp[lane] = v;
-    }
-    __syncthreads();
-    const int base = w ? s_warp[w - 1] : 0;
-    total = s_warp[nw - 1];
-    __syncthreads();
-    return base + pre;
-}
-
 __device__ __forceinline__ int block_sum(int v, int *s_warp) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
 #pragma unroll
@@ -1164,9 +1134,80 @@ __device__ __forceinline__ int block_sum(int v, int *s_warp) {
     return t;
 }
 
+/* Sum of v over this thread and all threads after it in the block. */
+__device__ __forceinline__ int block_suffix_sum(int v, int *s_warp) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int incl = v;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        const int t = __shfl_down_sync(0xffffffffu, incl, m);
+        if (lane + m < 32) incl += t;
+    }
+    if (lane == 0) s_warp[w] = incl;                     /* warp total */
+    __syncthreads();
+    for (int i = w + 1; i < nw; i++) incl += s_warp[i];
+    __syncthreads();
+    return incl;
+}
+
+/* Writes, in row order, the rows r < n whose key(r) > T, and the first
+ * `allow` rows whose key(r) == T, to kept[]; returns how many.  Each warp
+ * takes a contiguous range of rows, 32 at a time, so the counting is two
+ * ballots per 32 rows, the only block-wide step is one exchange of the warps'
+ * counts, and the indices go out as coalesced stores. */
+template <class KeyOf>
+__device__ __forceinline__ int ordered_keep(int n, uint32_t T, int allow, int32_t *kept, KeyOf key) {
+    __shared__ int s_gt[32], s_eq[32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int per_w = ((n + nw - 1) / nw + 31) & ~31;
+    const int r0 = min(n, w * per_w), r1 = min(n, r0 + per_w);
+    const unsigned lt = (1u << lane) - 1u;
+    int gt = 0, eq = 0;
+    for (int b = r0; b < r1; b += 64) {                  /* 2 chunks of 32 rows in flight */
+        uint32_t kk[2];
+#pragma unroll
+        for (int q = 0; q < 2; q++) kk[q] = b + 32 * q + lane < r1 ? key(b + 32 * q + lane) : 0u;
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            const bool in = b + 32 * q + lane < r1;
+            gt += __popc(__ballot_sync(0xffffffffu, in && kk[q] > T));
+            eq += __popc(__ballot_sync(0xffffffffu, in && kk[q] == T));
+        }
+    }
+    if (lane == 0) { s_gt[w] = gt; s_eq[w] = eq; }
+    __syncthreads();
+    int gt_before = 0, eq_before = 0, gt_all = 0, eq_all = 0;
+    for (int i = 0; i < nw; i++) {
+        const int g = s_gt[i], e = s_eq[i];
+        if (i < w) { gt_before += g; eq_before += e; }
+        gt_all += g;
+        eq_all += e;
+    }
+    const int al = max(allow, 0);
+    int out = gt_before + min(eq_before, al);
+    int eqr = eq_before;
+    for (int b = r0; b < r1; b += 64) {
+        uint32_t kk[2];
+#pragma unroll
+        for (int q = 0; q < 2; q++) kk[q] = b + 32 * q + lane < r1 ? key(b + 32 * q + lane) : 0u;
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            const int r = b + 32 * q + lane;
+            const bool e = r < r1 && kk[q] == T;
+            const unsigned em = __ballot_sync(0xffffffffu, e);
+            const bool kp = r < r1 && (kk[q] > T || (e && eqr + __popc(em & lt) < al));
+            const unsigned km = __ballot_sync(0xffffffffu, kp);
+            if (kp) kept[out + __popc(km & lt)] = r;
+            out += __popc(km);
+            eqr += __popc(em);
+        }
+    }
+    return gt_all + min(eq_all, al);
+}
+
 template <bool FUSED>
-__global__ void __launch_bounds__(SELECT_THREADS) k_select(const SelectArgs a) {
-    __shared__ int s_hist[256];
+__global__ void __launch_bounds__(SELECT_THREADS, 2) k_select(const SelectArgs a) {
+    __shared__ int s_hist[4096];
     __shared__ int s_warp[32];
     __shared__ int s_bc[2];
     const int u = blockIdx.x, tid = threadIdx.x, bd = blockDim.x;
@@ -1175,20 +1216,49 @@ __global__ void __launch_bounds__(SELECT_THREADS) k_select(const SelectArgs a) {
     int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
     const bool prot_on = a.window > 0 || a.sink > 0;
 
+    /* keys, SB rows per thread in flight (the loads are L2 round trips) */
+    constexpr int SB = 2;
     int prot = 0;
-    for (int r = tid; r < n; r += bd) {
-        float x;
-        if constexpr (FUSED) x = group_zmax(a.raw, a.raw_stride, a.ms, a.G, u, r);
-        else x = a.scores[(int64_t)u * a.score_stride + r];
-        uint32_t k = score_key(x);
-        if (prot_on) {
-            const int p = a.pos[a.pos_shared ? (int64_t)r : (int64_t)u * a.pos_cells + r];
-            if ((a.sink > 0 && p < a.sink) || (a.window > 0 && p >= a.cur_pos - a.window)) {
+    for (int rb = tid; rb < n; rb += SB * bd) {
+        float x[SB];
+#pragma unroll
+        for (int j = 0; j < SB; j++) x[j] = 0.f;
+        if constexpr (FUSED) {
+            /* z-score max over the group, as group_zmax (triattention.c:240-247) */
+            for (int g = 0; g < a.G; g++) {
+                const float2 m = a.ms[(int64_t)u * a.G + g];
+                const float *xr = a.raw + ((int64_t)u * a.G + g) * a.raw_stride;
+                float v[SB];
+#pragma unroll
+                for (int j = 0; j < SB; j++) v[j] = rb + j * bd < n ? xr[rb + j * bd] : 0.f;
+#pragma unroll
+                for (int j = 0; j < SB; j++) {
+                    const float z = __fdiv_rn(__fsub_rn(v[j], m.x), m.y);
+                    if (g == 0 || z > x[j]) x[j] = z;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < SB; j++)
+                if (rb + j * bd < n) x[j] = a.scores[(int64_t)u * a.score_stride + rb + j * bd];
+        }
+        int p[SB];
+#pragma unroll
+        for (int j = 0; j < SB; j++) {
+            const int r = rb + j * bd;
+            p[j] = prot_on && r < n ? a.pos[a.pos_shared ? (int64_t)r : (int64_t)u * a.pos_cells + r] : 0;
+        }
+#pragma unroll
+        for (int j = 0; j < SB; j++) {
+            const int r = rb + j * bd;
+            if (r >= n) continue;
+            uint32_t k = score_key(x[j]);
+            if (prot_on && ((a.sink > 0 && p[j] < a.sink) || (a.window > 0 && p[j] >= a.cur_pos - a.window))) {
                 k = 0xffffffffu;
                 prot++;
             }
+            keys[r] = k;
         }
-        keys[r] = k;
     }
     const int n_prot = prot_on ? block_sum(prot, s_warp) : 0;
     int keep = a.keep_req[u] > n_prot ? a.keep_req[u] : n_prot;
@@ -1205,35 +1275,39 @@ __global__ void __launch_bounds__(SELECT_THREADS) k_select(const SelectArgs a) {
         return;
     }
 
+    /* radix select of the keep-th largest key: digits of 12, 10 and 10 bits
+     * (a 12-bit first digit spreads the clustered high bits of the z-scores
+     * over enough bins that the shared-memory atomics rarely collide) */
     uint32_t prefix = 0;
     int need = keep;
-    for (int pass = 0; pass < 4; pass++) {
-        const int shift = 24 - 8 * pass;
-        for (int i = tid; i < 256; i += bd) s_hist[i] = 0;
+    for (int pass = 0; pass < 3; pass++) {
+        const int shift = pass == 0 ? 20 : (pass == 1 ? 10 : 0);
+        const int nb = pass == 0 ? 4096 : 1024;
+        const int hi = shift + 10;                       /* bits above this digit (pass > 0) */
+        for (int i = tid; i < nb; i += bd) s_hist[i] = 0;
         __syncthreads();
-        for (int r = tid; r < n; r += bd) {
-            const uint32_t k = keys[r];
-            if (pass == 0 || ((k ^ prefix) >> (shift + 8)) == 0u) atomicAdd(&s_hist[(k >> shift) & 255u], 1);
+        for (int rb = tid; rb < n; rb += 4 * bd) {
+            uint32_t kk[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) kk[j] = rb + j * bd < n ? keys[rb + j * bd] : 0u;
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (rb + j * bd < n && (pass == 0 || (kk[j] >> hi) == (prefix >> hi)))
+                    atomicAdd(&s_hist[(kk[j] >> shift) & (uint32_t)(nb - 1)], 1);
         }
         __syncthreads();
-        if (tid < 32) {
-            int loc[8], sum = 0;
-#pragma unroll
-            for (int i = 0; i < 8; i++) { loc[i] = s_hist[8 * tid + i]; sum += loc[i]; }
-            int incl = sum;      /* count in bins of this lane and all higher lanes */
-#pragma unroll
-            for (int m = 1; m < 32; m <<= 1) {
-                const int t = __shfl_down_sync(0xffffffffu, incl, m);
-                if (tid + m < 32) incl += t;
-            }
-            const int above = incl - sum;
-            const unsigned bal = __ballot_sync(0xffffffffu, above < need && need <= incl);
-            if (tid == __ffs(bal) - 1) {
-                int acc = above;
-                for (int i = 7; i >= 0; i--) {
-                    if (acc + loc[i] >= need) { s_bc[0] = 8 * tid + i; s_bc[1] = need - acc; break; }
-                    acc += loc[i];
-                }
+        /* thread t owns bins [t*c, t*c + c); count of keys in bins >= its first */
+        const int c = (nb + bd - 1) / bd;
+        int own = 0;
+        for (int i = 0; i < c; i++) own += tid * c + i < nb ? s_hist[tid * c + i] : 0;
+        const int incl = block_suffix_sum(own, s_warp);
+        const int above = incl - own;
+        if (above < need && need <= incl) {
+            int acc = above;
+            for (int i = c - 1; i >= 0; i--) {
+                const int h = tid * c + i < nb ? s_hist[tid * c + i] : 0;
+                if (acc + h >= need) { s_bc[0] = tid * c + i; s_bc[1] = need - acc; break; }
+                acc += h;
             }
         }
         __syncthreads();
@@ -1241,21 +1315,9 @@ __global__ void __launch_bounds__(SELECT_THREADS) k_select(const SelectArgs a) {
         need = s_bc[1];
         __syncthreads();
     }
-
-    int run_eq = 0, run_kept = 0;
-    for (int base = 0; base < n; base += bd) {
-        const int r = base + tid;
-        const uint32_t k = r < n ? keys[r] : 0u;
-        const bool eq = r < n && k == prefix;
-        int tot_eq, tot_k;
-        const int eq_rank = run_eq + block_excl_scan(eq, s_warp, tot_eq);
-        const bool kp = r < n && (k > prefix || (eq && eq_rank < need));
-        const int dst = run_kept + block_excl_scan(kp, s_warp, tot_k);
-        if (kp) kept[dst] = r;
-        run_eq += tot_eq;
-        run_kept += tot_k;
-    }
-    if (tid == 0) a.n_kept[u] = keep;
+    /* keys above the threshold, and the first `need` equal to it in row order */
+    const int kept_n = ordered_keep(n, prefix, need, kept, [&](int r) { return keys[r]; });
+    if (tid == 0) a.n_kept[u] = kept_n;
 }
 
 /* ------------------------------------------------------------------ */
@@ -1319,20 +1381,8 @@ __global__ void __launch_bounds__(SELECT_THREADS) k_select_key(const KeyArgs a) 
     before = block_sum(before, s_warp);
     const int64_t left = a.tie_allow - before;
     const int allow = left <= 0 ? 0 : (int)min(left, (int64_t)a.counts_in[a.u0 + u]);
-    int run_eq = 0, run_kept = 0;
-    for (int base = 0; base < n; base += bd) {
-        const int r = base + tid;
-        const uint32_t k = r < n ? score_key(sc[r]) : 0u;
-        const bool eq = r < n && k == a.key;
-        int tot_eq, tot_k;
-        const int eq_rank = run_eq + block_excl_scan(eq, s_warp, tot_eq);
-        const bool kp = r < n && (k > a.key || (eq && eq_rank < allow));
-        const int dst = run_kept + block_excl_scan(kp, s_warp, tot_k);
-        if (kp) kept[dst] = r;
-        run_eq += tot_eq;
-        run_kept += tot_k;
-    }
-    if (tid == 0) a.n_kept[u] = run_kept;
+    const int kept_n = ordered_keep(n, a.key, allow, kept, [&](int r) { return score_key(sc[r]); });
+    if (tid == 0) a.n_kept[u] = kept_n;
 }
 
 /* ------------------------------------------------------------------ */
