@@ -326,8 +326,16 @@ struct WsPlan {
     __host__ __device__ int stage_bytes(int fc) const { return k_bytes() + tab_bytes(fc) + pos_ints * 4; }
     __host__ __device__ int ring_bytes() const { return WS_POS_RING * pos_ints * 4; }
     __host__ __device__ int part_floats() const { return WS_CWARPS * tile * 8 * gp(); }   /* one buffer */
+    /* q terms of one (pair slot i, lane group j): 3 x G packed pairs, the stride
+     * padded to an odd number of 16-byte units so that the 8 lane groups' loads
+     * fall in distinct bank groups */
+    __host__ __device__ int qj_bytes() const {
+        int b = (24 * G + 15) / 16;
+        return 16 * (b | 1);
+    }
+    __host__ __device__ int q_bytes() const { return WS_CWARPS * 4 * 8 * qj_bytes(); }   /* all warps */
     __host__ __device__ int total(int fc) const {
-        return stages * stage_bytes(fc) + ring_bytes() + part_slots * part_floats() * 4 +
+        return stages * stage_bytes(fc) + ring_bytes() + part_slots * part_floats() * 4 + q_bytes() +
                (2 * stages + WS_POS_RING + 2 * part_slots) * 8;
     }
 };
@@ -466,7 +474,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
     uint8_t *stages = smem;
     int32_t *ring = reinterpret_cast<int32_t *>(smem + S * stage_bytes);              /* [WS_POS_RING][pos_ints] */
     float *part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ring) + plan.ring_bytes());
-    uint64_t *full = reinterpret_cast<uint64_t *>(part + plan.part_slots * plan.part_floats());
+    uint8_t *qsm = reinterpret_cast<uint8_t *>(part + plan.part_slots * plan.part_floats());   /* [warp][i][j] q terms */
+    uint64_t *full = reinterpret_cast<uint64_t *>(qsm + plan.q_bytes());
     uint64_t *empty = full + S;
     uint64_t *posbar = empty + S;
     uint64_t *pfull = posbar + WS_POS_RING;              /* partials of an item written */
@@ -498,7 +507,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
     if (warp < WS_CWARPS) {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(WS_CONSUMER_REGS));
         /* ---------------- consumers ---------------- */
-        const int j = lane & 7, cs4 = lane >> 3;             /* chunk group (pairs 8j..8j+7), cell of the pass */
+        const int j = lane & 7, cs4 = lane >> 3;             /* lane group (pairs 4j..4j+3), cell of the pass */
         const int wph = max(1, WS_CWARPS / KV);              /* warps per head */
         const bool active = warp < KV * wph;
         const int h = active ? warp % KV : 0, sub = warp / KV;
@@ -507,7 +516,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         int toff[QPL];                                       /* bytes of chunk 4j+i within a table row */
 #pragma unroll
         for (int i = 0; i < QPL; i++) toff[i] = 16 * tab_chunk(4 * j + i);
-        f2_t qr[G][QPL], qi[G][QPL], qx[G][QPL];
+        const int qj = plan.qj_bytes();
+        uint8_t *qw = qsm + warp * (QPL * 8 * qj);          /* this warp's q terms: [i][j] x (qr, qi, qx) x G */
         int cur_l = -1;
         int l = 0, t = 0;                                    /* layer and tile of item k (no divisions) */
         if (n_mine > 0) { l = it0 / a.tiles_per_layer; t = it0 - l * a.tiles_per_layer; }
@@ -531,45 +541,50 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
             f2_t acc[WS_CPL][G];
             int ts[WS_CPL];
             if (cb < cend) {
-                if (l != cur_l) {                                  /* this lane's q terms for layer l */
+                if (l != cur_l) {                                  /* the head's q terms for layer l */
                     cur_l = l;
                     const int ml = a.layer0 + l, mh = a.head0 + h;
                     const float *src = a.q + ((size_t)(ml * a.H + mh * G) * 3) * FC;
-#pragma unroll
-                    for (int g = 0; g < G; g++)
-#pragma unroll
-                        for (int i = 0; i < QPL; i++) {
-                            const int q = 4 * j + i;
-                            const float2 r = *reinterpret_cast<const float2 *>(src + g * 3 * FC + 2 * q);
-                            const float2 m = *reinterpret_cast<const float2 *>(src + g * 3 * FC + FC + 2 * q);
-                            qr[g][i] = pk2(r.x * inv17, r.y * inv17);
-                            qi[g][i] = pk2(m.x * inv17, m.y * inv17);
-                            const float2 x = *reinterpret_cast<const float2 *>(src + g * 3 * FC + 2 * FC + 2 * q);
-                            qx[g][i] = pk2(x.x * a.qx_scale, x.y * a.qx_scale);
-                        }
+                    __syncwarp();
+                    for (int e = lane; e < QPL * 8 * 3 * G; e += 32) {
+                        const int g = e % G, comp = (e / G) % 3, jj = (e / (3 * G)) % 8, i = e / (24 * G);
+                        const float2 v = *reinterpret_cast<const float2 *>(src + g * 3 * FC + comp * FC + 2 * (4 * jj + i));
+                        const float sc = comp == 2 ? a.qx_scale : inv17;
+                        *reinterpret_cast<f2_t *>(qw + (i * 8 + jj) * qj + (comp * G + g) * 8) = pk2(v.x * sc, v.y * sc);
+                    }
+                    __syncwarp();
                 }
                 const int hoff = h * a.row_bytes;
+                const uint8_t *row[WS_CPL], *trow[WS_CPL];
+                uint4 kr4[WS_CPL], ki4[WS_CPL];                    /* f16: each cell's 8 real / 8 imag halves of this lane */
 #pragma unroll
                 for (int e = 0; e < WS_CPL; e++) {
                     const int c = cb + 4 * e + cs4;
                     const bool valid = c < cend;
                     ts[e] = valid ? slot[a.pos_shared ? c : h * SC_T + c] : -1;
-                    const uint8_t *row = sb + (valid ? c : cb) * a.cell_stride + hoff;
-                    const uint8_t *trow = tab + max(ts[e], 0) * (FC * 8);
-                    uint4 kr4, ki4;                                /* f16: this lane's 8 real / 8 imag halves */
+                    row[e] = sb + (valid ? c : cb) * a.cell_stride + hoff;
+                    trow[e] = tab + max(ts[e], 0) * (FC * 8);
                     if constexpr (KT == KT_F16) {
-                        kr4 = *reinterpret_cast<const uint4 *>(row + 16 * j);
-                        ki4 = *reinterpret_cast<const uint4 *>(row + 2 * FC + 16 * j);
+                        kr4[e] = *reinterpret_cast<const uint4 *>(row[e] + 16 * j);
+                        ki4[e] = *reinterpret_cast<const uint4 *>(row[e] + 2 * FC + 16 * j);
                     }
+                }
+                /* pair slot i of every cell, then the next: only one slot's q terms are live */
 #pragma unroll
-                    for (int i = 0; i < QPL; i++) {
-                        const ulonglong2 cs = *reinterpret_cast<const ulonglong2 *>(trow + toff[i]);  /* (C, S) */
+                for (int i = 0; i < QPL; i++) {
+                    f2_t qr[G], qi[G], qx[G];
+                    const f2_t *qp = reinterpret_cast<const f2_t *>(qw + (i * 8 + j) * qj);
+#pragma unroll
+                    for (int g = 0; g < G; g++) { qr[g] = qp[g]; qi[g] = qp[G + g]; qx[g] = qp[2 * G + g]; }
+#pragma unroll
+                    for (int e = 0; e < WS_CPL; e++) {
+                        const ulonglong2 cs = *reinterpret_cast<const ulonglong2 *>(trow[e] + toff[i]);  /* (C, S) */
                         f2_t kr, ki;
                         if constexpr (KT == KT_F16) {
-                            kr = h2_to_f2(i == 0 ? kr4.x : i == 1 ? kr4.y : i == 2 ? kr4.z : kr4.w);
-                            ki = h2_to_f2(i == 0 ? ki4.x : i == 1 ? ki4.y : i == 2 ? ki4.z : ki4.w);
+                            kr = h2_to_f2(i == 0 ? kr4[e].x : i == 1 ? kr4[e].y : i == 2 ? kr4[e].z : kr4[e].w);
+                            ki = h2_to_f2(i == 0 ? ki4[e].x : i == 1 ? ki4[e].y : i == 2 ? ki4[e].z : ki4[e].w);
                         } else {
-                            row_pair<KT, FC>(row, 4 * j + i, kr, ki);
+                            row_pair<KT, FC>(row[e], 4 * j + i, kr, ki);
                         }
                         const f2_t X = fma2(cs.x, kr, mul2(cs.y, ki));
                         const f2_t Y = sub2(mul2(cs.x, ki), mul2(cs.y, kr));
@@ -579,9 +594,9 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                         const f2_t ka = pk2(sqrt_approx(m0), sqrt_approx(m1));
 #pragma unroll
                         for (int g = 0; g < G; g++) {
-                            acc[e][g] = i == 0 ? mul2(qr[g][i], X) : fma2(qr[g][i], X, acc[e][g]);
-                            acc[e][g] = fma2(qi[g][i], Y, acc[e][g]);
-                            acc[e][g] = fma2(qx[g][i], ka, acc[e][g]);
+                            acc[e][g] = i == 0 ? mul2(qr[g], X) : fma2(qr[g], X, acc[e][g]);
+                            acc[e][g] = fma2(qi[g], Y, acc[e][g]);
+                            acc[e][g] = fma2(qx[g], ka, acc[e][g]);
                         }
                     }
                 }
@@ -837,8 +852,47 @@ __device__ __forceinline__ bool zs_ok(int x, int sg) {
 }
 
 /* The record of one segment whose lane elements are xs[0..3] (dead ones 0),
- * under the binade of `approx`; the result is the same in every lane. */
+ * under the binade of `approx`; the result is the same in every lane.  The
+ * common segment (no tie, no element too large for the grid) takes the short
+ * path; a vote sends the others through zs_record_exact. */
+__device__ __noinline__ ZsRec zs_record_exact(float x0, float x1, float x2, float x3, double approx);
 __device__ __forceinline__ ZsRec zs_record(const float (&xs)[4], double approx) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t ab = __float_as_uint((float)approx);
+    const int exb = (ab >> 23) & 0xff;
+    if (exb == 0 || exb == 255 || exb < 23) return ZsRec{ZS_SLOW, 0, 0, 0};   /* uniform across the warp */
+    const float scale = __int_as_float((150 - (exb - 127)) << 23);
+    int lsum = 0, pl = 0x7fffffff, ph = -0x7fffffff - 1;
+    bool special = false;
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+        const float q = xs[t] * scale;
+        const float f = __fadd_rn(q, 0x1.8p23f);
+        const float fr = __fsub_rn(q, __fsub_rn(f, 0x1.8p23f));
+        special |= !(fabsf(q) < 0x1p22f) || fabsf(fr) == 0.5f;
+        lsum += (int)((uint32_t)__float_as_int(f) - 0x4b400000u);
+        pl = min(pl, lsum);
+        ph = max(ph, lsum);
+    }
+    if (__any_sync(0xffffffffu, special)) return zs_record_exact(xs[0], xs[1], xs[2], xs[3], approx);
+    int incl = lsum;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, m);
+        if (lane >= m) incl += y;
+    }
+    const int ex = incl - lsum;
+    ZsRec r;
+    r.f = (uint32_t)exb;
+    r.delta = __shfl_sync(0xffffffffu, incl, 31);
+    r.pmin = __reduce_min_sync(0xffffffffu, ex + pl);
+    r.pmax = __reduce_max_sync(0xffffffffu, ex + ph);
+    return r;
+}
+
+/* zs_record for segments with ties or elements off the grid (out of line: rare). */
+__device__ __noinline__ ZsRec zs_record_exact(float x0, float x1, float x2, float x3, double approx) {
+    const float xs[4] = {x0, x1, x2, x3};
     const int lane = threadIdx.x & 31;
     const uint32_t ab = __float_as_uint((float)approx);
     const int exb = (ab >> 23) & 0xff;
@@ -1216,6 +1270,10 @@ __global__ void __launch_bounds__(SELECT_THREADS, 2) k_select(const SelectArgs a
     int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
     const bool prot_on = a.window > 0 || a.sink > 0;
 
+    /* (mean, std) of the unit's query heads */
+    __shared__ float2 s_zs[TRIA_MAX_GQA];
+    if (FUSED && tid < a.G) s_zs[tid] = a.ms[(int64_t)u * a.G + tid];
+    __syncthreads();
     /* keys, SB rows per thread in flight (the loads are L2 round trips) */
     constexpr int SB = 2;
     int prot = 0;
@@ -1226,7 +1284,7 @@ __global__ void __launch_bounds__(SELECT_THREADS, 2) k_select(const SelectArgs a
         if constexpr (FUSED) {
             /* z-score max over the group, as group_zmax (triattention.c:240-247) */
             for (int g = 0; g < a.G; g++) {
-                const float2 m = a.ms[(int64_t)u * a.G + g];
+                const float2 m = s_zs[g];
                 const float *xr = a.raw + ((int64_t)u * a.G + g) * a.raw_stride;
                 float v[SB];
 #pragma unroll
