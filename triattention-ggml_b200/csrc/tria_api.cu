@@ -629,8 +629,8 @@ static int launch_select(tria_ctx *c, const tria_kv_view *v, const int32_t *n_ro
             a->n_rows[u] = n_rows[u0 + u];
             a->keep_req[u] = keep[u0 + u];
         }
-        if (fused) k_select<true><<<units, SELECT_THREADS, 0, st>>>(*a);
-        else k_select<false><<<units, SELECT_THREADS, 0, st>>>(*a);
+        if (fused) k_select<true><<<units, SELECT_BLOCK, 0, st>>>(*a);
+        else k_select<false><<<units, SELECT_BLOCK, 0, st>>>(*a);
         delete a;
         CUDA_TRY(cudaGetLastError());
         c->launches++;
@@ -1425,7 +1425,7 @@ extern "C" TRIA_API int tria_select_noalloc(const float *scores, int64_t score_s
         a.n_rows[u] = n_rows[u];
         a.keep_req[u] = keep[u];
     }
-    k_select<false><<<units, SELECT_THREADS, 0, (cudaStream_t)stream>>>(a);
+    k_select<false><<<units, SELECT_BLOCK, 0, (cudaStream_t)stream>>>(a);
     CUDA_TRY(cudaGetLastError());
     return TRIA_OK;
 }

@@ -50,6 +50,7 @@ constexpr int N_OFF = 17;
 constexpr int SCORE_THREADS = 256;
 constexpr int SCORE_CHUNK = 256;       /* cells per CTA (per layer) */
 constexpr int SELECT_THREADS = 1024;
+constexpr int SELECT_BLOCK = 768;                 /* k_select: two blocks per SM at 40 registers */
 
 /* ------------------------------------------------------------------ */
 /* Delta table                                                          */
@@ -1217,12 +1218,12 @@ __device__ __forceinline__ int ordered_keep(int n, uint32_t T, int allow, int32_
     const int r0 = min(n, w * per_w), r1 = min(n, r0 + per_w);
     const unsigned lt = (1u << lane) - 1u;
     int gt = 0, eq = 0;
-    for (int b = r0; b < r1; b += 64) {                  /* 2 chunks of 32 rows in flight */
-        uint32_t kk[2];
+    for (int b = r0; b < r1; b += 128) {                 /* 4 chunks of 32 rows in flight */
+        uint32_t kk[4];
 #pragma unroll
-        for (int q = 0; q < 2; q++) kk[q] = b + 32 * q + lane < r1 ? key(b + 32 * q + lane) : 0u;
+        for (int q = 0; q < 4; q++) kk[q] = b + 32 * q + lane < r1 ? key(b + 32 * q + lane) : 0u;
 #pragma unroll
-        for (int q = 0; q < 2; q++) {
+        for (int q = 0; q < 4; q++) {
             const bool in = b + 32 * q + lane < r1;
             gt += __popc(__ballot_sync(0xffffffffu, in && kk[q] > T));
             eq += __popc(__ballot_sync(0xffffffffu, in && kk[q] == T));
@@ -1240,12 +1241,12 @@ __device__ __forceinline__ int ordered_keep(int n, uint32_t T, int allow, int32_
     const int al = max(allow, 0);
     int out = gt_before + min(eq_before, al);
     int eqr = eq_before;
-    for (int b = r0; b < r1; b += 64) {
-        uint32_t kk[2];
+    for (int b = r0; b < r1; b += 128) {
+        uint32_t kk[4];
 #pragma unroll
-        for (int q = 0; q < 2; q++) kk[q] = b + 32 * q + lane < r1 ? key(b + 32 * q + lane) : 0u;
+        for (int q = 0; q < 4; q++) kk[q] = b + 32 * q + lane < r1 ? key(b + 32 * q + lane) : 0u;
 #pragma unroll
-        for (int q = 0; q < 2; q++) {
+        for (int q = 0; q < 4; q++) {
             const int r = b + 32 * q + lane;
             const bool e = r < r1 && kk[q] == T;
             const unsigned em = __ballot_sync(0xffffffffu, e);
@@ -1260,7 +1261,7 @@ __device__ __forceinline__ int ordered_keep(int n, uint32_t T, int allow, int32_
 }
 
 template <bool FUSED>
-__global__ void __launch_bounds__(SELECT_THREADS, 2) k_select(const SelectArgs a) {
+__global__ void __launch_bounds__(SELECT_BLOCK, 2) k_select(const SelectArgs a) {
     __shared__ int s_hist[4096];
     __shared__ int s_warp[32];
     __shared__ int s_bc[2];
@@ -1274,8 +1275,9 @@ __global__ void __launch_bounds__(SELECT_THREADS, 2) k_select(const SelectArgs a
     __shared__ float2 s_zs[TRIA_MAX_GQA];
     if (FUSED && tid < a.G) s_zs[tid] = a.ms[(int64_t)u * a.G + tid];
     __syncthreads();
-    /* keys, SB rows per thread in flight (the loads are L2 round trips) */
-    constexpr int SB = 2;
+    /* keys: SB rows per thread and GB query heads at a time, so that SB x GB
+     * loads are in flight (the raw scores are L2 / DRAM round trips) */
+    constexpr int SB = 4, GB = 2;
     int prot = 0;
     for (int rb = tid; rb < n; rb += SB * bd) {
         float x[SB];
@@ -1283,16 +1285,23 @@ __global__ void __launch_bounds__(SELECT_THREADS, 2) k_select(const SelectArgs a
         for (int j = 0; j < SB; j++) x[j] = 0.f;
         if constexpr (FUSED) {
             /* z-score max over the group, as group_zmax (triattention.c:240-247) */
-            for (int g = 0; g < a.G; g++) {
-                const float2 m = s_zs[g];
-                const float *xr = a.raw + ((int64_t)u * a.G + g) * a.raw_stride;
-                float v[SB];
+            for (int g0 = 0; g0 < a.G; g0 += GB) {
+                float v[GB][SB];
 #pragma unroll
-                for (int j = 0; j < SB; j++) v[j] = rb + j * bd < n ? xr[rb + j * bd] : 0.f;
+                for (int gg = 0; gg < GB; gg++) {
+                    const float *xr = a.raw + ((int64_t)u * a.G + g0 + gg) * a.raw_stride;
 #pragma unroll
-                for (int j = 0; j < SB; j++) {
-                    const float z = __fdiv_rn(__fsub_rn(v[j], m.x), m.y);
-                    if (g == 0 || z > x[j]) x[j] = z;
+                    for (int j = 0; j < SB; j++) v[gg][j] = g0 + gg < a.G && rb + j * bd < n ? xr[rb + j * bd] : 0.f;
+                }
+#pragma unroll
+                for (int gg = 0; gg < GB; gg++) {
+                    if (g0 + gg >= a.G) break;
+                    const float2 m = s_zs[g0 + gg];
+#pragma unroll
+                    for (int j = 0; j < SB; j++) {
+                        const float z = __fdiv_rn(__fsub_rn(v[gg][j], m.x), m.y);
+                        if (g0 + gg == 0 || z > x[j]) x[j] = z;
+                    }
                 }
             }
         } else {
@@ -1344,12 +1353,12 @@ __global__ void __launch_bounds__(SELECT_THREADS, 2) k_select(const SelectArgs a
         const int hi = shift + 10;                       /* bits above this digit (pass > 0) */
         for (int i = tid; i < nb; i += bd) s_hist[i] = 0;
         __syncthreads();
-        for (int rb = tid; rb < n; rb += 4 * bd) {
-            uint32_t kk[4];
+        for (int rb = tid; rb < n; rb += 8 * bd) {
+            uint32_t kk[8];
 #pragma unroll
-            for (int j = 0; j < 4; j++) kk[j] = rb + j * bd < n ? keys[rb + j * bd] : 0u;
+            for (int j = 0; j < 8; j++) kk[j] = rb + j * bd < n ? keys[rb + j * bd] : 0u;
 #pragma unroll
-            for (int j = 0; j < 4; j++)
+            for (int j = 0; j < 8; j++)
                 if (rb + j * bd < n && (pass == 0 || (kk[j] >> hi) == (prefix >> hi)))
                     atomicAdd(&s_hist[(kk[j] >> shift) & (uint32_t)(nb - 1)], 1);
         }
