@@ -180,10 +180,21 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- CPU baseline
 
-def cpu_step_rate(c, stats_path, n_units, seed=0, threads=None, data=None):
+def cpu_data(c, n_units, seed=0):
+    """Seeded K and V caches (numpy, the bench distributions) covering n_units units."""
+    n_layer = max(1, (n_units + c["KV"] - 1) // c["KV"])
+    if c["type"] == workloads.TYPE_F16:
+        return (workloads.f16_cache(n_layer, c["n"], c["KV"], c["hd"], seed=seed),
+                workloads.f16_cache(n_layer, c["n"], c["KV"], c["hd"], seed=seed + 1))
+    return (workloads.q8_0_cache(n_layer, c["n"], c["KV"], c["hd"], seed=seed),
+            workloads.q8_0_cache(n_layer, c["n"], c["KV"], c["hd"], seed=seed + 1))
+
+
+def cpu_step_rate(c, stats_path, n_units, seed=0, threads=None, data=None, rows=None):
     """Run the reference CPU step (reference tria_score_kv_head + oracle select and
-    compact, pthreads over units) on n_units units of the workload.
-    Returns (rows/s, seconds, threads, kind)."""
+    compact, pthreads over units) on n_units units of the workload, each on its
+    first `rows` rows (all of them by default; a shorter prefix keeps the same
+    kept fraction).  Returns (rows/s, seconds, threads, kind)."""
     import oracle_py
     orc = oracle_py.Oracle()
     if oracle_py.RefLib.available():
@@ -192,22 +203,14 @@ def cpu_step_rate(c, stats_path, n_units, seed=0, threads=None, data=None):
     else:
         load, free, fn, kind = orc.load, orc.free, orc.score_fn_ptr, "port"
     threads = threads or len(os.sched_getaffinity(0))
-    hd, KV, n = c["hd"], c["KV"], c["n"]
+    hd, KV, n_all = c["hd"], c["KV"], c["n"]
+    n = n_all if rows is None else min(int(rows), n_all)
     rb = workloads.row_bytes(c["type"], hd)
-    n_layer = max(1, (n_units + KV - 1) // KV)
-    if data is None:
-        if c["type"] == workloads.TYPE_F16:
-            K = workloads.f16_cache(n_layer, n, KV, hd, seed=seed)
-            V = workloads.f16_cache(n_layer, n, KV, hd, seed=seed + 1)
-        else:
-            K = workloads.q8_0_cache(n_layer, n, KV, hd, seed=seed)
-            V = workloads.q8_0_cache(n_layer, n, KV, hd, seed=seed + 1)
-    else:
-        K, V = data
+    K, V = data if data is not None else cpu_data(c, n_units, seed)
     Ko, Vo = np.zeros_like(K), np.zeros_like(V)
-    pos = np.arange(n, dtype=np.int32)
-    pos_o = np.zeros((n_units, n), np.int32)
-    keep = workloads.layer_keep(n, budget_rows(c), c["ramp"])
+    pos = np.arange(n_all, dtype=np.int32)
+    pos_o = np.zeros((n_units, n_all), np.int32)
+    keep = workloads.layer_keep(n, max(1, budget_rows(c) * n // n_all), c["ramp"])
     st = load(stats_path)
     units = []
     for u in range(n_units):
@@ -230,6 +233,9 @@ def write_stats(c, td):
     return path
 
 
+REF_RUN_S = 90.0     # wall-time budget of a whole --impl reference run
+
+
 def run_reference(args):
     """--impl reference: the reference's CPU path on the host cores, rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
@@ -239,19 +245,29 @@ def run_reference(args):
     threads = len(os.sched_getaffinity(0))
     with tempfile.TemporaryDirectory() as td:
         path = write_stats(c, td)
-        # size one step to ~4 s of wall time: one probe unit per thread first
-        _, dt1, _, _ = cpu_step_rate(c, path, min(threads, c["L"] * c["KV"]), seed=1, threads=threads)
-        per_unit_thread = dt1 / max(1, -(-min(threads, c["L"] * c["KV"]) // threads))
-        units = int(max(1, min(c["L"] * c["KV"], threads * max(1, round(4.0 / per_unit_thread)))))
+        # The whole run (warm-up and timed steps) is held to about REF_RUN_S
+        # seconds: a step is a bounded sample of the workload.  One unit per
+        # thread is timed first; a step is a whole number of such rounds when
+        # that fits, else one unit per thread on a prefix of its rows.
+        n_probe = min(threads, c["L"] * c["KV"])
+        data = cpu_data(c, n_probe, seed=1)
+        _, dt1, _, _ = cpu_step_rate(c, path, n_probe, threads=threads, data=data)
+        per_step = max(0.05, min(4.0, REF_RUN_S / max(1, args.warmup + args.steps)))
+        rounds = int(max(1, per_step // dt1))
+        units = min(c["L"] * c["KV"], n_probe * rounds)
+        if units > n_probe:
+            data = cpu_data(c, units, seed=1)
+        rows = c["n"] if per_step >= dt1 else max(1024, int(c["n"] * per_step / dt1) // 256 * 256)
         rates = []
         kind = "reference"
         for i in range(args.warmup + args.steps):
-            r, dt, th, kind = cpu_step_rate(c, path, units, seed=2 + i, threads=threads)
+            r, dt, th, kind = cpu_step_rate(c, path, units, threads=threads, data=data, rows=rows)
             if i >= args.warmup:
                 rates.append((r, dt))
     value = statistics.median(r for r, _ in rates)
     ms = statistics.median(dt for _, dt in rates) * 1e3
-    sample = f"{units} of {c['L'] * c['KV']} (layer, kv-head) units x {c['n']} rows per step"
+    sample = (f"{units} of {c['L'] * c['KV']} (layer, kv-head) units x {rows} of {c['n']} rows per step "
+              f"(the same seeded data every step; run held to ~{REF_RUN_S:.0f} s)")
     line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
