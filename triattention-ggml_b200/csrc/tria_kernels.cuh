@@ -288,7 +288,6 @@ constexpr int WS_THREADS = (WS_CWARPS + 4) * 32;   /* + a producer warpgroup, on
  * most the launch total, or the increase would wait forever; the host checks
  * the compiled register count before every launch. */
 constexpr int WS_LAUNCH_REGS = 168;
-constexpr int WS_PREFETCH = 2;          /* items whose K tiles are prefetched to L2 beyond the stages */
 constexpr int WS_PRODUCER_REGS = 72;
 constexpr int WS_CONSUMER_REGS = 216;
 constexpr int WS_RWARPS = 3;           /* reducer warps: the producer warpgroup's other three */
@@ -363,10 +362,6 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
-}
-/* Bulk prefetch global -> L2 (no shared memory, no completion to wait for). */
-__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
@@ -656,22 +651,11 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                 bulk_g2s(ring + (kk % WS_POS_RING) * plan.pos_ints + lane * SC_T, src, pb, bar);
             }
         };
-        /* K tile of item kk -> L2 ahead of its copy: the copy into a stage can only
-         * start when the consumers release that stage, so with few stages a copy
-         * straight from DRAM would leave them waiting for its latency */
-        auto prefetch_k = [&](int kk) {
-            if (lane != 0 || kk >= n_mine) return;
-            int l, c0;
-            const int cells = item_of(kk, l, c0);
-            if (cells > 0) bulk_prefetch_l2(a.k[l] + (int64_t)c0 * a.cell_stride, (uint32_t)(cells * a.cell_stride));
-        };
         int pos_issued = 0;                              /* items whose positions were requested */
         for (; pos_issued < min(WS_POS_RING - 1, n_mine); pos_issued++) fetch_pos(pos_issued);
-        for (int kk = S; kk < S + WS_PREFETCH - 1; kk++) prefetch_k(kk);
         int k = 0;
         for (; k < n_mine && !s_abort; k++) {
             const int st = k % S;
-            prefetch_k(k + S + WS_PREFETCH - 1);
             if (pos_issued < n_mine) fetch_pos(pos_issued++);   /* ring slot of item k-1: done with */
             if (!mbar_wait(&posbar[k % WS_POS_RING], (uint32_t)((k / WS_POS_RING) & 1)) ||
                 !mbar_wait(&empty[st], (uint32_t)(((k / S) & 1) ^ 1))) {
@@ -836,7 +820,10 @@ struct ZArgs {
     int32_t n_rows[TRIA_MAX_UNITS];
 };
 
-constexpr int ZS_SEG = 128;                        /* elements per segment: 4 per lane */
+constexpr int ZS_SEG = 128;                        /* elements per segment */
+constexpr int ZS_EPL = ZS_SEG / 32;                /* consecutive elements per lane */
+static_assert(ZS_EPL % 4 == 0, "whole float4 per lane");
+struct ZsVals { float v[ZS_EPL]; };
 constexpr int ZS_WARPS = 4;
 constexpr int ZS_WIN = 32;                         /* segments per window: one walk batch */
 constexpr int ZS_SPW = ZS_WIN / ZS_WARPS;          /* segments per warp per window */
@@ -856,8 +843,9 @@ __device__ __forceinline__ bool zs_ok(int x, int sg) {
  * under the binade of `approx`; the result is the same in every lane.  The
  * common segment (no tie, no element too large for the grid) takes the short
  * path; a vote sends the others through zs_record_exact. */
-__device__ __noinline__ ZsRec zs_record_exact(float x0, float x1, float x2, float x3, double approx);
-__device__ __forceinline__ ZsRec zs_record(const float (&xs)[4], double approx) {
+__device__ __noinline__ ZsRec zs_record_exact(ZsVals xv, double approx);
+__device__ __forceinline__ ZsRec zs_record(const ZsVals &xv, double approx) {
+    const float (&xs)[ZS_EPL] = xv.v;
     const int lane = threadIdx.x & 31;
     const uint32_t ab = __float_as_uint((float)approx);
     const int exb = (ab >> 23) & 0xff;
@@ -866,7 +854,7 @@ __device__ __forceinline__ ZsRec zs_record(const float (&xs)[4], double approx) 
     int lsum = 0, pl = 0x7fffffff, ph = -0x7fffffff - 1;
     bool special = false;
 #pragma unroll
-    for (int t = 0; t < 4; t++) {
+    for (int t = 0; t < ZS_EPL; t++) {
         const float q = xs[t] * scale;
         const float f = __fadd_rn(q, 0x1.8p23f);
         const float fr = __fsub_rn(q, __fsub_rn(f, 0x1.8p23f));
@@ -875,7 +863,7 @@ __device__ __forceinline__ ZsRec zs_record(const float (&xs)[4], double approx) 
         pl = min(pl, lsum);
         ph = max(ph, lsum);
     }
-    if (__any_sync(0xffffffffu, special)) return zs_record_exact(xs[0], xs[1], xs[2], xs[3], approx);
+    if (__any_sync(0xffffffffu, special)) return zs_record_exact(xv, approx);
     int incl = lsum;
 #pragma unroll
     for (int m = 1; m < 32; m <<= 1) {
@@ -892,8 +880,8 @@ __device__ __forceinline__ ZsRec zs_record(const float (&xs)[4], double approx) 
 }
 
 /* zs_record for segments with ties or elements off the grid (out of line: rare). */
-__device__ __noinline__ ZsRec zs_record_exact(float x0, float x1, float x2, float x3, double approx) {
-    const float xs[4] = {x0, x1, x2, x3};
+__device__ __noinline__ ZsRec zs_record_exact(ZsVals xv, double approx) {
+    const float (&xs)[ZS_EPL] = xv.v;
     const int lane = threadIdx.x & 31;
     const uint32_t ab = __float_as_uint((float)approx);
     const int exb = (ab >> 23) & 0xff;
@@ -902,7 +890,7 @@ __device__ __noinline__ ZsRec zs_record_exact(float x0, float x1, float x2, floa
     int lsum = 0, pl = 0x7fffffff, ph = -0x7fffffff - 1, tc = 0, tp1 = 0, tp2 = 0;
     bool out = false;
 #pragma unroll
-    for (int t = 0; t < 4; t++) {
+    for (int t = 0; t < ZS_EPL; t++) {
         const float q = xs[t] * scale;
         const bool o = !(fabsf(q) < 0x1p22f);
         const float f = __fadd_rn(q, 0x1.8p23f);
@@ -1041,22 +1029,28 @@ __device__ float zs_pass(const float *x, int n, Val val, float *s_sum, ZsRec *s_
     for (int w0 = 0; w0 < nseg; w0 += ZS_WIN) {
         const int wcnt = min(ZS_WIN, nseg - w0);
         /* this warp's segments warp, warp + ZS_WARPS, ... of the window: values and sums */
-        float xs[ZS_SPW][4];
+        ZsVals xs[ZS_SPW];
 #pragma unroll
         for (int j = 0; j < ZS_SPW; j++) {
             const int sl = warp + ZS_WARPS * j;
-            const int e = (w0 + sl) * ZS_SEG + 4 * lane;
-            const int live = sl < wcnt ? max(0, min(4, n - e)) : 0;
-            float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (live > 0) w = *reinterpret_cast<const float4 *>(x + e);   /* e + 3 < stride: e % 4 == 0, e < n */
-            xs[j][0] = live > 0 ? val(w.x) : 0.f;
-            xs[j][1] = live > 1 ? val(w.y) : 0.f;
-            xs[j][2] = live > 2 ? val(w.z) : 0.f;
-            xs[j][3] = live > 3 ? val(w.w) : 0.f;
+            const int e0 = (w0 + sl) * ZS_SEG + ZS_EPL * lane;
+#pragma unroll
+            for (int v4 = 0; v4 < ZS_EPL; v4 += 4) {
+                const int e = e0 + v4;
+                const int live = sl < wcnt ? max(0, min(4, n - e)) : 0;
+                float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (live > 0) w = *reinterpret_cast<const float4 *>(x + e);   /* e + 3 < stride: e % 4 == 0, e < n */
+                xs[j].v[v4 + 0] = live > 0 ? val(w.x) : 0.f;
+                xs[j].v[v4 + 1] = live > 1 ? val(w.y) : 0.f;
+                xs[j].v[v4 + 2] = live > 2 ? val(w.z) : 0.f;
+                xs[j].v[v4 + 3] = live > 3 ? val(w.w) : 0.f;
+            }
         }
 #pragma unroll
         for (int j = 0; j < ZS_SPW; j++) {
-            float t = (xs[j][0] + xs[j][1]) + (xs[j][2] + xs[j][3]);
+            float t = 0.f;
+#pragma unroll
+            for (int q = 0; q < ZS_EPL; q++) t += xs[j].v[q];
 #pragma unroll
             for (int m = 16; m; m >>= 1) t += __shfl_xor_sync(0xffffffffu, t, m);
             const int sl = warp + ZS_WARPS * j;
@@ -1065,8 +1059,10 @@ __device__ float zs_pass(const float *x, int n, Val val, float *s_sum, ZsRec *s_
         __syncthreads();        /* window sums; the exact sum at the window start; the walk of the last window is over */
 #pragma unroll
         for (int j = 0; j < ZS_SPW; j++)                /* values for the walk's plain adds */
-            *reinterpret_cast<float4 *>(s_vals + (warp + ZS_WARPS * j) * ZS_SEG + 4 * lane) =
-                make_float4(xs[j][0], xs[j][1], xs[j][2], xs[j][3]);
+#pragma unroll
+            for (int v4 = 0; v4 < ZS_EPL; v4 += 4)
+                *reinterpret_cast<float4 *>(s_vals + (warp + ZS_WARPS * j) * ZS_SEG + ZS_EPL * lane + v4) =
+                    make_float4(xs[j].v[v4], xs[j].v[v4 + 1], xs[j].v[v4 + 2], xs[j].v[v4 + 3]);
         /* approximate prefix sums at each segment start (one segment per lane) */
         const double a0 = lane < wcnt ? (double)s_sum[lane] : 0.0;
         double inc = a0;
