@@ -20,8 +20,9 @@
  *                  into the table (rel_r cos - rel_i sin summed over o).
  *   k_znorm_seg    mean and variance bit-identical to the reference's
  *                  sequential fp32 chains (triattention.c:228-236): segments
- *                  of 128 elements precomputed as ulp-grid translations, then
- *                  walked 32 segments per step; IEEE div/sqrt, std clamp 1e-6.
+ *                  of 256 elements precomputed as ulp-grid translations, then
+ *                  walked a window of 16 segments per step; IEEE div/sqrt,
+ *                  std clamp 1e-6.
  *   k_select       z-score max over the group (triattention.c:240-247), an
  *                  order-preserving 32-bit key, radix select (12-, 10- and
  *                  10-bit digits) of the keep-th largest key, ties to the
@@ -820,12 +821,12 @@ struct ZArgs {
     int32_t n_rows[TRIA_MAX_UNITS];
 };
 
-constexpr int ZS_SEG = 128;                        /* elements per segment */
+constexpr int ZS_SEG = 256;                        /* elements per segment */
 constexpr int ZS_EPL = ZS_SEG / 32;                /* consecutive elements per lane */
 static_assert(ZS_EPL % 4 == 0, "whole float4 per lane");
 struct ZsVals { float v[ZS_EPL]; };
 constexpr int ZS_WARPS = 4;
-constexpr int ZS_WIN = 32;                         /* segments per window: one walk batch */
+constexpr int ZS_WIN = 16;                         /* segments per window: one walk batch, 16 KB staged */
 constexpr int ZS_SPW = ZS_WIN / ZS_WARPS;          /* segments per warp per window */
 constexpr uint32_t ZS_SLOW = 1u << 13;             /* record flag: walk the segment element by element */
 
