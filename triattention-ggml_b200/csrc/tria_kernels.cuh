@@ -1274,7 +1274,7 @@ __global__ void __launch_bounds__(SELECT_BLOCK, 2) k_select(const SelectArgs a) 
     __syncthreads();
     /* keys: SB rows per thread and GB query heads at a time, so that SB x GB
      * loads are in flight (the raw scores are L2 / DRAM round trips) */
-    constexpr int SB = 4, GB = 2;
+    constexpr int SB = 8, GB = 1;
     int prot = 0;
     for (int rb = tid; rb < n; rb += SB * bd) {
         float x[SB];
