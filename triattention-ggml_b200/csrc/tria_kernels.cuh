@@ -411,22 +411,27 @@ __device__ __forceinline__ f2_t h2_to_f2(uint32_t h) {
     return r;
 }
 
-/* Frequency pair q (dims 2q, 2q+1) of the real and imaginary halves of a staged row. */
-template <int KT, int FC>
-__device__ __forceinline__ void row_pair(const uint8_t *row, int q, f2_t &kr, f2_t &ki) {
-    if constexpr (KT == KT_F16) {
-        kr = h2_to_f2(*reinterpret_cast<const uint32_t *>(row + 4 * q));
-        ki = h2_to_f2(*reinterpret_cast<const uint32_t *>(row + 2 * FC + 4 * q));
-    } else {                                             /* q8_0 block {f16 d; int8 q[32]} */
-        const int dr = 2 * q, dm = FC + 2 * q;
-        const uint8_t *br = row + (dr >> 5) * 34, *bm = row + (dm >> 5) * 34;
-        const float sr = __half2float(*reinterpret_cast<const __half *>(br));
-        const float sm = __half2float(*reinterpret_cast<const __half *>(bm));
-        const char2 vr = *reinterpret_cast<const char2 *>(br + 2 + (dr & 31));
-        const char2 vm = *reinterpret_cast<const char2 *>(bm + 2 + (dm & 31));
-        kr = pk2((float)vr.x * sr, (float)vr.y * sr);
-        ki = pk2((float)vm.x * sm, (float)vm.y * sm);
-    }
+/* q8_0 block {f16 d; int8 q[32]}: a lane's 8 consecutive values starting at
+ * offset o (o % 8 == 0; 2-byte aligned in shared memory) as two words with the
+ * sign bits flipped (byte = q + 128), and the block's scale twice. */
+__device__ __forceinline__ uint4 q8_lane_load(const uint8_t *blk, int o) {
+    const uint16_t *p = reinterpret_cast<const uint16_t *>(blk + 2 + o);
+    const uint32_t w0 = (uint32_t)p[0] | ((uint32_t)p[1] << 16);
+    const uint32_t w1 = (uint32_t)p[2] | ((uint32_t)p[3] << 16);
+    const uint32_t d = __float_as_uint(__half2float(*reinterpret_cast<const __half *>(blk)));
+    return make_uint4(w0 ^ 0x80808080u, w1 ^ 0x80808080u, d, d);
+}
+/* Values 2i and 2i+1 of a q8_lane_load, dequantised as the reference does,
+ * (float)q * d with one rounding.  A byte permute places q + 128 in the low
+ * byte of the float 2^23 (0x4B000000), so subtracting 2^23 + 128 gives q
+ * exactly, without a conversion instruction. */
+__device__ __forceinline__ f2_t q8_pair(const uint4 &w, int i) {
+    const uint32_t word = i < 2 ? w.x : w.y;
+    const uint32_t b = (uint32_t)(2 * i) & 3u;
+    const float lo = __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7650u | b));
+    const float hi = __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7650u | (b + 1u)));
+    const f2_t q = sub2(pk2(lo, hi), pk2(8388736.f, 8388736.f));
+    return mul2(q, pk2(__uint_as_float(w.z), __uint_as_float(w.w)));
 }
 
 /*
@@ -553,7 +558,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                 }
                 const int hoff = h * a.row_bytes;
                 const uint8_t *row[WS_CPL], *trow[WS_CPL];
-                uint4 kr4[WS_CPL], ki4[WS_CPL];                    /* f16: each cell's 8 real / 8 imag halves of this lane */
+                uint4 kr4[WS_CPL], ki4[WS_CPL];                    /* each cell's 8 real / 8 imag values of this lane */
 #pragma unroll
                 for (int e = 0; e < WS_CPL; e++) {
                     const int c = cb + 4 * e + cs4;
@@ -564,6 +569,9 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                     if constexpr (KT == KT_F16) {
                         kr4[e] = *reinterpret_cast<const uint4 *>(row[e] + 16 * j);
                         ki4[e] = *reinterpret_cast<const uint4 *>(row[e] + 2 * FC + 16 * j);
+                    } else {                                       /* q8_0: dims 8j.. in block j/4, imag two blocks on */
+                        kr4[e] = q8_lane_load(row[e] + 34 * (j >> 2), 8 * (j & 3));
+                        ki4[e] = q8_lane_load(row[e] + 34 * (2 + (j >> 2)), 8 * (j & 3));
                     }
                 }
                 /* pair slot i of every cell, then the next: only one slot's q terms are live */
@@ -581,7 +589,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                             kr = h2_to_f2(i == 0 ? kr4[e].x : i == 1 ? kr4[e].y : i == 2 ? kr4[e].z : kr4[e].w);
                             ki = h2_to_f2(i == 0 ? ki4[e].x : i == 1 ? ki4[e].y : i == 2 ? ki4[e].z : ki4[e].w);
                         } else {
-                            row_pair<KT, FC>(row[e], 4 * j + i, kr, ki);
+                            kr = q8_pair(kr4[e], i);
+                            ki = q8_pair(ki4[e], i);
                         }
                         const f2_t X = fma2(cs.x, kr, mul2(cs.y, ki));
                         const f2_t Y = sub2(mul2(cs.x, ki), mul2(cs.y, kr));
@@ -1272,33 +1281,30 @@ __global__ void __launch_bounds__(SELECT_BLOCK, 2) k_select(const SelectArgs a) 
     __shared__ float2 s_zs[TRIA_MAX_GQA];
     if (FUSED && tid < a.G) s_zs[tid] = a.ms[(int64_t)u * a.G + tid];
     __syncthreads();
-    /* keys: SB rows per thread and GB query heads at a time, so that SB x GB
-     * loads are in flight (the raw scores are L2 / DRAM round trips) */
-    constexpr int SB = 8, GB = 1;
+    /* keys, SB rows per thread in flight (the raw scores are L2 / DRAM round
+     * trips).  Fused: two 16-byte loads of 4 consecutive rows per query head
+     * (raw rows are 16-byte aligned and padded to a multiple of 64 floats, so a
+     * load that starts below n stays inside the row). */
+    constexpr int SB = 8;
     int prot = 0;
-    for (int rb = tid; rb < n; rb += SB * bd) {
+    for (int rb = FUSED ? 4 * tid : tid; rb < n; rb += SB * bd) {
+        auto row_of = [&](int j) { return FUSED ? rb + (j & 3) + (j >> 2) * 4 * bd : rb + j * bd; };
         float x[SB];
 #pragma unroll
         for (int j = 0; j < SB; j++) x[j] = 0.f;
         if constexpr (FUSED) {
             /* z-score max over the group, as group_zmax (triattention.c:240-247) */
-            for (int g0 = 0; g0 < a.G; g0 += GB) {
-                float v[GB][SB];
+            for (int g = 0; g < a.G; g++) {
+                const float *xr = a.raw + ((int64_t)u * a.G + g) * a.raw_stride;
+                const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 v0 = rb < n ? *reinterpret_cast<const float4 *>(xr + rb) : z4;
+                const float4 v1 = rb + 4 * bd < n ? *reinterpret_cast<const float4 *>(xr + rb + 4 * bd) : z4;
+                const float v[SB] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                const float2 m = s_zs[g];
 #pragma unroll
-                for (int gg = 0; gg < GB; gg++) {
-                    const float *xr = a.raw + ((int64_t)u * a.G + g0 + gg) * a.raw_stride;
-#pragma unroll
-                    for (int j = 0; j < SB; j++) v[gg][j] = g0 + gg < a.G && rb + j * bd < n ? xr[rb + j * bd] : 0.f;
-                }
-#pragma unroll
-                for (int gg = 0; gg < GB; gg++) {
-                    if (g0 + gg >= a.G) break;
-                    const float2 m = s_zs[g0 + gg];
-#pragma unroll
-                    for (int j = 0; j < SB; j++) {
-                        const float z = __fdiv_rn(__fsub_rn(v[gg][j], m.x), m.y);
-                        if (g0 + gg == 0 || z > x[j]) x[j] = z;
-                    }
+                for (int j = 0; j < SB; j++) {
+                    const float z = __fdiv_rn(__fsub_rn(v[j], m.x), m.y);
+                    if (g == 0 || z > x[j]) x[j] = z;
                 }
             }
         } else {
@@ -1309,12 +1315,12 @@ __global__ void __launch_bounds__(SELECT_BLOCK, 2) k_select(const SelectArgs a) 
         int p[SB];
 #pragma unroll
         for (int j = 0; j < SB; j++) {
-            const int r = rb + j * bd;
+            const int r = row_of(j);
             p[j] = prot_on && r < n ? a.pos[a.pos_shared ? (int64_t)r : (int64_t)u * a.pos_cells + r] : 0;
         }
 #pragma unroll
         for (int j = 0; j < SB; j++) {
-            const int r = rb + j * bd;
+            const int r = row_of(j);
             if (r >= n) continue;
             uint32_t k = score_key(x[j]);
             if (prot_on && ((a.sink > 0 && p[j] < a.sink) || (a.window > 0 && p[j] >= a.cur_pos - a.window))) {
