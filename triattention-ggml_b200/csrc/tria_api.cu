@@ -646,6 +646,14 @@ static int launch_compact(tria_ctx *c, const tria_kv_view *s, const tria_kv_view
     const int64_t rb = view_row_bytes(s->type, (int)c->hd);
     auto al = [](int64_t x) { return x & 15 ? (x & 7 ? 4 : 8) : 16; };
     int vec = std::min({al(rb), al(s->cell_stride), al(s->head_stride), al(d->cell_stride), al(d->head_stride)});
+    /* rows 8 bytes off 16-byte alignment whose source and destination share
+     * that offset for every head: 16-byte chunks plus one 8-byte piece */
+    bool split = vec == 8 && rb % 16 == 8 && s->cell_stride % 16 == 0 && d->cell_stride % 16 == 0 &&
+                 (s->head_stride - d->head_stride) % 16 == 0;
+    for (int l = 0; split && l < s->n_layer; l++) {
+        auto a16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
+        split = a16(s->k[l]) && a16(d->k[l]) && (!s->v || (a16(s->v[l]) && a16(d->v[l])));
+    }
     return for_layer_chunks(s, [&](int l0, int nl) -> int {
         CompactArgs *a = new (std::nothrow) CompactArgs;
         if (!a) FAIL(TRIA_ERR_NOMEM, "host allocation failed");
@@ -673,11 +681,12 @@ static int launch_compact(tria_ctx *c, const tria_kv_view *s, const tria_kv_view
         int max_rows = 0;
         for (int u = 0; u < units; u++) max_rows = std::max(max_rows, n_rows[u0 + u]);
         const int rows = rows_hint >= 0 ? std::min(rows_hint, max_rows) : max_rows;
-        const int64_t work = (int64_t)std::max(rows, 1) * (rb / vec);
+        const int64_t work = (int64_t)std::max(rows, 1) * (split ? rb / 16 + 1 : rb / vec);
         const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 1024));
         dim3 grid(gx, units);
         if (max_rows > 0) {
-            if (vec == 16) k_compact<16><<<grid, 256, 0, st>>>(*a);
+            if (split) k_compact_split<<<grid, 256, 0, st>>>(*a);
+            else if (vec == 16) k_compact<16><<<grid, 256, 0, st>>>(*a);
             else if (vec == 8) k_compact<8><<<grid, 256, 0, st>>>(*a);
             else k_compact<4><<<grid, 256, 0, st>>>(*a);
             c->launches++;

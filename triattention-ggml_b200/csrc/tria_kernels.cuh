@@ -1511,4 +1511,41 @@ __global__ void __launch_bounds__(256) k_compact(const CompactArgs a) {
     }
 }
 
+/* Stable gather for rows that are 8 bytes off 16-byte alignment (q8_0 rows of
+ * 136 bytes), when source and destination rows of a head share their
+ * alignment modulo 16: each row moves as rb / 16 chunks of 16 bytes and one
+ * 8-byte piece (at the start of the row when the head's rows begin 8 bytes
+ * off a 16-byte boundary, else at its end). */
+__global__ void __launch_bounds__(256) k_compact_split(const CompactArgs a) {
+    const int u = blockIdx.y;
+    const int l = u / a.n_head_kv, h = u - l * a.n_head_kv;
+    const int nk = a.n_kept[u];
+    const int nseg = a.row_bytes / 16 + 1;
+    const bool lead8 = (((int64_t)h * a.hs_s) & 15) != 0;
+    const int64_t total = (int64_t)nk * nseg;
+    const int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
+    const uint8_t *ks = a.ks[l] + (int64_t)h * a.hs_s;
+    uint8_t *kd = a.kd[l] + (int64_t)h * a.hs_d;
+    const uint8_t *vs = a.has_v ? a.vs[l] + (int64_t)h * a.hs_s : nullptr;
+    uint8_t *vd = a.has_v ? a.vd[l] + (int64_t)h * a.hs_d : nullptr;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int jrow = (int)(i / nseg);
+        const int sg = (int)(i - (int64_t)jrow * nseg);
+        const int r = kept[jrow];
+        const int64_t so = (int64_t)r * a.cs_s, d0 = (int64_t)jrow * a.cs_d;
+        if (sg < nseg - 1) {
+            const int off = (lead8 ? 8 : 0) + 16 * sg;
+            *reinterpret_cast<uint4 *>(kd + d0 + off) = *reinterpret_cast<const uint4 *>(ks + so + off);
+            if (vs) *reinterpret_cast<uint4 *>(vd + d0 + off) = *reinterpret_cast<const uint4 *>(vs + so + off);
+        } else {
+            const int off = lead8 ? 0 : a.row_bytes - 8;
+            *reinterpret_cast<uint2 *>(kd + d0 + off) = *reinterpret_cast<const uint2 *>(ks + so + off);
+            if (vs) *reinterpret_cast<uint2 *>(vd + d0 + off) = *reinterpret_cast<const uint2 *>(vs + so + off);
+        }
+        if (sg == 0)
+            a.pos_d[(int64_t)u * a.cells_d + jrow] = a.pos_s[a.pos_shared_s ? (int64_t)r : (int64_t)u * a.cells_s + r];
+    }
+}
+
 }  // namespace tria
