@@ -446,11 +446,13 @@ static WsPlan ws_plan(const tria_ctx *c, const tria_kv_view *v) {
     if (c->G != 1 && c->G != 2 && c->G != 4 && c->G != 5 && c->G != 6) return p;
     p.cell_bytes = (int)v->cell_stride;
     p.G = (int)c->G;
+    /* per-head positions: table rows straight from L2 (16-cell tiles, no staged table) */
+    p.direct = v->pos_shared ? 0 : 1;
     /* the largest tile, then the most partial buffers, then the most stages that fit */
-    for (int tile = c->G <= 4 ? WS_TILE_MAX : 16; tile >= 16; tile /= 2) {   /* 32 cells: too many registers above G = 4 */
+    for (int tile = c->G <= 4 && !p.direct ? WS_TILE_MAX : 16; tile >= 16; tile /= 2) {   /* 32 cells: too many registers above G = 4 */
         p.tile = tile;
-        p.tab_rows = v->pos_shared ? tile : tile * v->n_head_kv;
-        p.pos_ints = p.tab_rows;
+        p.pos_ints = v->pos_shared ? tile : tile * v->n_head_kv;
+        p.tab_rows = p.direct ? 0 : p.pos_ints;
         for (int ps = 2; ps >= 1; ps--)
             for (int s = 4; s >= 2; s--) {
                 p.stages = s;
@@ -462,9 +464,9 @@ static WsPlan ws_plan(const tria_ctx *c, const tria_kv_view *v) {
     return p;
 }
 
-template <int KT, int G, int T>
+template <int KT, int G, int T, bool DT = false>
 static int launch_ws_inst(const TmaScoreArgs &a, const WsPlan &plan, int grid, cudaStream_t st) {
-    auto fn = k_score_ws<KT, G, T>;
+    auto fn = k_score_ws<KT, G, T, DT>;
     /* the setmaxnreg split inside the kernel assumes this launch allocation */
     static int regs = -1;
     if (regs < 0) {
@@ -485,6 +487,16 @@ static int launch_ws_inst(const TmaScoreArgs &a, const WsPlan &plan, int grid, c
 template <int KT>
 static int launch_ws_g(int G, const TmaScoreArgs &a, const WsPlan &plan, int grid, cudaStream_t st) {
     const bool t32 = plan.tile == 32;
+    if (plan.direct) {
+        switch (G) {
+            case 1: return launch_ws_inst<KT, 1, 16, true>(a, plan, grid, st);
+            case 2: return launch_ws_inst<KT, 2, 16, true>(a, plan, grid, st);
+            case 4: return launch_ws_inst<KT, 4, 16, true>(a, plan, grid, st);
+            case 5: return launch_ws_inst<KT, 5, 16, true>(a, plan, grid, st);
+            case 6: return launch_ws_inst<KT, 6, 16, true>(a, plan, grid, st);
+            default: FAIL(TRIA_ERR_UNSUPPORTED, "k_score_ws: gqa %d not instantiated", G);
+        }
+    }
     switch (G) {
         case 1: return t32 ? launch_ws_inst<KT, 1, 32>(a, plan, grid, st) : launch_ws_inst<KT, 1, 16>(a, plan, grid, st);
         case 2: return t32 ? launch_ws_inst<KT, 2, 32>(a, plan, grid, st) : launch_ws_inst<KT, 2, 16>(a, plan, grid, st);

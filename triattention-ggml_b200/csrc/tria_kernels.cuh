@@ -321,6 +321,7 @@ struct TmaScoreArgs {
  * (GP = G padded to 4 or 8) in one of part_slots partial buffers. */
 struct WsPlan {
     int tile, stages, cell_bytes, tab_rows, pos_ints, G, part_slots;
+    int direct;                      /* table rows read from global memory, not staged (tab_rows == 0) */
     __host__ __device__ int gp() const { return G <= 4 ? 4 : 8; }
     __host__ __device__ int k_bytes() const { return tile * cell_bytes; }
     __host__ __device__ int tab_bytes(int fc) const { return tab_rows * fc * 8; }
@@ -464,7 +465,7 @@ __device__ __forceinline__ f2_t q8_pair(const uint4 &w, int i) {
  * code sits after its own setmaxnreg so the compiler budgets it alone.
  * Every wait is bounded (ST_TIMEOUT).
  */
-template <int KT, int G, int SC_T>
+template <int KT, int G, int SC_T, bool DT>
 __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a, const WsPlan plan) {
     constexpr int FC = 64, NQ = FC / 2, QPL = 4;        /* pairs per lane */
     constexpr int WS_CPL = SC_T / 4;                     /* cells per lane: a warp's tile cells in one pass */
@@ -565,7 +566,9 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                     const bool valid = c < cend;
                     ts[e] = valid ? slot[a.pos_shared ? c : h * SC_T + c] : -1;
                     row[e] = sb + (valid ? c : cb) * a.cell_stride + hoff;
-                    trow[e] = tab + max(ts[e], 0) * (FC * 8);
+                    /* staged: the row's table row in the stage; direct: its table row in global memory */
+                    trow[e] = DT ? reinterpret_cast<const uint8_t *>(a.table) + (int64_t)max(ts[e], 0) * (FC * 8)
+                                 : tab + max(ts[e], 0) * (FC * 8);
                     if constexpr (KT == KT_F16) {
                         kr4[e] = *reinterpret_cast<const uint4 *>(row[e] + 16 * j);
                         ki4[e] = *reinterpret_cast<const uint4 *>(row[e] + 2 * FC + 16 * j);
@@ -574,16 +577,30 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                         ki4[e] = q8_lane_load(row[e] + 34 * (2 + (j >> 2)), 8 * (j & 3));
                     }
                 }
+                /* direct: each cell's table chunk of the next pair slot is in flight
+                 * from L2 while this slot computes */
+                ulonglong2 tb[2][DT ? WS_CPL : 1];
+                if constexpr (DT) {
+#pragma unroll
+                    for (int e = 0; e < WS_CPL; e++) tb[0][e] = __ldg(reinterpret_cast<const ulonglong2 *>(trow[e] + toff[0]));
+                }
                 /* pair slot i of every cell, then the next: only one slot's q terms are live */
 #pragma unroll
                 for (int i = 0; i < QPL; i++) {
+                    if constexpr (DT) {
+                        if (i + 1 < QPL) {
+#pragma unroll
+                            for (int e = 0; e < WS_CPL; e++)
+                                tb[(i + 1) & 1][e] = __ldg(reinterpret_cast<const ulonglong2 *>(trow[e] + toff[i + 1]));
+                        }
+                    }
                     f2_t qr[G], qi[G], qx[G];
                     const f2_t *qp = reinterpret_cast<const f2_t *>(qw + (i * 8 + j) * qj);
 #pragma unroll
                     for (int g = 0; g < G; g++) { qr[g] = qp[g]; qi[g] = qp[G + g]; qx[g] = qp[2 * G + g]; }
 #pragma unroll
                     for (int e = 0; e < WS_CPL; e++) {
-                        const ulonglong2 cs = *reinterpret_cast<const ulonglong2 *>(trow[e] + toff[i]);  /* (C, S) */
+                        const ulonglong2 cs = DT ? tb[i & 1][e] : *reinterpret_cast<const ulonglong2 *>(trow[e] + toff[i]);  /* (C, S) */
                         f2_t kr, ki;
                         if constexpr (KT == KT_F16) {
                             kr = h2_to_f2(i == 0 ? kr4[e].x : i == 1 ? kr4[e].y : i == 2 ? kr4[e].z : kr4[e].w);
@@ -705,14 +722,14 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                 const unsigned startm = __ballot_sync(0xffffffffu, start);
                 const unsigned after = lane < 31 ? contm >> (lane + 1) : 0u;
                 const int len = start ? __ffs(~after) : 0;         /* this run's cells, from its first lane */
-                if (start) {                                 /* rows ascend with position or with delta */
+                if (!DT && start) {                          /* rows ascend with position or with delta */
                     mbar_expect(&full[st], (uint32_t)len * FC * 8);
                     bulk_g2s(tab + (hh * SC_T + lane) * NQ, a.table + (a.by_pos ? d : d - len + 1) * NQ,
                              (uint32_t)len * FC * 8, &full[st]);
                 }
                 const int s0 = max(0, 31 - __clz(startm & ((2u << lane) - 1u)));   /* first lane of my run */
                 const int rl = __shfl_sync(0xffffffffu, len, s0);
-                if (act) slot[hh * SC_T + lane] = ok ? hh * SC_T + (a.by_pos ? lane : 2 * s0 + rl - 1 - lane) : -1;
+                if (act) slot[hh * SC_T + lane] = !ok ? -1 : DT ? (int32_t)d : hh * SC_T + (a.by_pos ? lane : 2 * s0 + rl - 1 - lane);
                 if (lane == 0 && __popc(okm) != cells) atomicOr(a.status, ST_POSITION);
                 __syncwarp();
             }
