@@ -447,7 +447,11 @@ __device__ __forceinline__ f2_t q8_pair(const uint4 &w, int i) {
  * are consecutive (a fresh cache, appended rows), else one copy per row; it
  * records each row's table slot in the stage.  The stage's `full` barrier
  * completes when all bytes landed.  Few large copies matter: the copy engine
- * streams 32 KB tiles at HBM speed but not sixteen 2 KB pieces.
+ * streams 32 KB tiles at HBM speed but not sixteen 2 KB pieces.  With DT
+ * (per-head positions, where every (cell, head) row has its own table row
+ * and short runs) no table rows are staged: the producer writes each row's
+ * table index into the stage and the consumers load their table chunks from
+ * global memory (L2), one pair slot ahead of the math.
  *
  * Each consumer warp scores one kv head, all cells of the tile (32, or 16
  * when per-head table rows make a 32-cell stage too large) in one pass:
