@@ -317,17 +317,19 @@ struct TmaScoreArgs {
 };
 
 /* Shared-memory plan of k_score_ws, shared by host and device.  Per work item
- * the consumers leave, for each of its rows, 8 lanes x GP partial sums
- * (GP = G padded to 4 or 8) in one of part_slots partial buffers. */
+ * the consumers leave, for each of its rows, 8 lanes x lp() partial sums in
+ * one of part_slots partial buffers: for G <= 4 a cell's lanes first swap
+ * halves pairwise, so a lane leaves 2 sums (query heads 0,1 or 2,3 over two
+ * lanes); above that every lane leaves 8 (G padded to 8). */
 struct WsPlan {
     int tile, stages, cell_bytes, tab_rows, pos_ints, G, part_slots;
     int direct;                      /* table rows read from global memory, not staged (tab_rows == 0) */
-    __host__ __device__ int gp() const { return G <= 4 ? 4 : 8; }
+    __host__ __device__ int lp() const { return G <= 4 ? 2 : 8; }
     __host__ __device__ int k_bytes() const { return tile * cell_bytes; }
     __host__ __device__ int tab_bytes(int fc) const { return tab_rows * fc * 8; }
     __host__ __device__ int stage_bytes(int fc) const { return k_bytes() + tab_bytes(fc) + pos_ints * 4; }
     __host__ __device__ int ring_bytes() const { return WS_POS_RING * pos_ints * 4; }
-    __host__ __device__ int part_floats() const { return WS_CWARPS * tile * 8 * gp(); }   /* one buffer */
+    __host__ __device__ int part_floats() const { return WS_CWARPS * tile * 8 * lp(); }   /* one buffer */
     /* q terms of one (pair slot i, lane group j): 3 x G packed pairs, the stride
      * padded to an odd number of 16-byte units so that the 8 lane groups' loads
      * fall in distinct bank groups */
@@ -454,17 +456,19 @@ __device__ __forceinline__ f2_t q8_pair(const uint4 &w, int i) {
  * global memory (L2), one pair slot ahead of the math.
  *
  * Each consumer warp scores one kv head, all cells of the tile (32, or 16
- * when per-head table rows make a 32-cell stage too large) in one pass:
- * 8 lanes per cell, lane j owning the frequency pairs 8j..8j+7 (table
- * chunks 4j..4j+3) and SC_T / 4 cells, so a cell's 8 lanes load 128
- * contiguous bytes of K per instruction and, through the chunk rotation of
- * tab_chunk(), eight distinct bank groups of its table row.  The lane's
- * q-centre terms (pre-scaled by 1/17) and norm terms stay in registers for
- * the whole layer; the math runs as packed f32x2 FMAs.  Each lane leaves
- * its G partial sums per cell in a partial buffer (8 lanes x GP floats per
- * row) and moves on; the producer warpgroup's other three warps sum each
- * row's 8 partials and write the raw scores, so no consumer waits on a
- * shuffle reduction.  The producer warpgroup runs on WS_PRODUCER_REGS
+ * for G > 4 and for per-head positions) in one pass: 8 lanes per cell, lane
+ * j owning the frequency pairs 4j..4j+3 (dims 8j..8j+7, table chunks
+ * 4j..4j+3) and SC_T / 4 cells, so a cell's 8 lanes load 128 contiguous
+ * bytes of K per instruction and, through the chunk rotation of
+ * tab_chunk(), eight distinct bank groups of its table row.  The head's
+ * q-centre terms (pre-scaled by 1/17) and norm terms for the layer sit in
+ * shared memory; the lane walks pair slot -> cells, so one slot's terms are
+ * in registers at a time, and the math runs as packed f32x2 FMAs.  Each
+ * lane leaves its G partial sums per cell in a partial buffer (for G <= 4
+ * after one pairwise swap with lane j^4: 2 floats a lane) and moves on; the
+ * producer warpgroup's other three warps sum each row's partials and write
+ * the raw scores, so no consumer waits on a full shuffle reduction.
+ * The producer warpgroup runs on WS_PRODUCER_REGS
  * registers and hands the rest to the consumers (setmaxnreg); each role's
  * code sits after its own setmaxnreg so the compiler budgets it alone.
  * Every wait is bounded (ST_TIMEOUT).
@@ -487,7 +491,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
     uint64_t *posbar = empty + S;
     uint64_t *pfull = posbar + WS_POS_RING;              /* partials of an item written */
     uint64_t *pfree = pfull + plan.part_slots;           /* partials of an item reduced */
-    const int P = plan.part_slots, GP = plan.gp();
+    const int P = plan.part_slots, LP = plan.lp();
     __shared__ volatile int s_abort;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -641,18 +645,24 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
 #pragma unroll
                 for (int e = 0; e < WS_CPL; e++) {
                     const int c = cb + 4 * e + cs4;
-                    if (c < cend) {
-                        /* a row outside the table scores 0 (the status says so) */
-                        float v[8];
+                    /* a row outside the table scores 0 (the status says so) */
+                    float v[8];
 #pragma unroll
-                        for (int g = 0; g < 8; g++) {
-                            float a0 = 0.f, a1 = 0.f;
-                            if (g < G) upk(acc[e][g], a0, a1);
-                            v[g] = ts[e] >= 0 ? a0 + a1 : 0.f;
-                        }
-                        float4 *dst = reinterpret_cast<float4 *>(pb + ((h * SC_T + c) * 8 + j) * GP);
+                    for (int g = 0; g < 8; g++) {
+                        float a0 = 0.f, a1 = 0.f;
+                        if (g < G) upk(acc[e][g], a0, a1);
+                        v[g] = ts[e] >= 0 ? a0 + a1 : 0.f;
+                    }
+                    if constexpr (G <= 4) {
+                        /* lanes j and j^4 of the cell: j keeps heads 0,1 (j < 4) or 2,3 and adds its partner's */
+                        const bool hi = (j & 4) != 0;
+                        const float k0 = (hi ? v[2] : v[0]) + __shfl_xor_sync(0xffffffffu, hi ? v[0] : v[2], 4);
+                        const float k1 = (hi ? v[3] : v[1]) + __shfl_xor_sync(0xffffffffu, hi ? v[1] : v[3], 4);
+                        if (c < cend) *reinterpret_cast<float2 *>(pb + ((h * SC_T + c) * 8 + j) * 2) = make_float2(k0, k1);
+                    } else if (c < cend) {
+                        float4 *dst = reinterpret_cast<float4 *>(pb + ((h * SC_T + c) * 8 + j) * 8);
                         dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-                        if (G > 4) dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+                        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
                     }
                 }
             }
@@ -776,17 +786,26 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                 const int h = r / SC_T, c = r - h * SC_T;
                 const int u = l * KV + h;
                 if (c >= min(cells, a.n_rows[u] - c0)) continue;
-                const float *row = pb + r * 8 * GP;
+                const float *row = pb + r * 8 * LP;
                 float sum[8];
 #pragma unroll
                 for (int g = 0; g < 8; g++) sum[g] = 0.f;
+                if constexpr (G <= 4) {
+                    /* lanes 0-3 left heads 0,1, lanes 4-7 heads 2,3, two floats each */
 #pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const int jj = (i + lane) & 7;               /* rotated: a phase's 8 rows hit 8 bank groups */
+                    for (int i = 0; i < 4; i++) {
+                        const int q = (i + lane) & 3;                /* rotated over the row's four 16-byte chunks */
+                        const float4 w = *reinterpret_cast<const float4 *>(row + 4 * q);
+                        const float s0 = w.x + w.z, s1 = w.y + w.w;
+                        if (q < 2) { sum[0] += s0; sum[1] += s1; } else { sum[2] += s0; sum[3] += s1; }
+                    }
+                } else {
 #pragma unroll
-                    for (int g4 = 0; g4 < 8; g4 += 4) {
-                        if (g4 < GP) {
-                            const float4 w = *reinterpret_cast<const float4 *>(row + jj * GP + g4);
+                    for (int i = 0; i < 8; i++) {
+                        const int jj = (i + lane) & 7;               /* rotated: a phase's 8 rows hit 8 bank groups */
+#pragma unroll
+                        for (int g4 = 0; g4 < 8; g4 += 4) {
+                            const float4 w = *reinterpret_cast<const float4 *>(row + jj * 8 + g4);
                             sum[g4] += w.x; sum[g4 + 1] += w.y; sum[g4 + 2] += w.z; sum[g4 + 3] += w.w;
                         }
                     }
