@@ -696,8 +696,17 @@ static int launch_compact(tria_ctx *c, const tria_kv_view *s, const tria_kv_view
         const int64_t work = (int64_t)std::max(rows, 1) * (split ? rb / 16 + 1 : rb / vec);
         const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 1024));
         dim3 grid(gx, units);
+        /* rows of 8, 16 or 32 aligned 16-byte chunks: a group of lanes per row */
+        const int ch = vec == 16 ? (int)(rb / 16) : 0;
+        const bool by_row = ch == 8 || ch == 16 || ch == 32;
+        if (by_row) {   /* 256 threads move 2 * 256 / ch rows per step */
+            grid.x = (unsigned)std::max<int64_t>(1, std::min<int64_t>(((int64_t)std::max(rows, 1) * ch + 511) / 512, 1024));
+        }
         if (max_rows > 0) {
             if (split) k_compact_split<<<grid, 256, 0, st>>>(*a);
+            else if (ch == 8) k_compact_rows<8><<<grid, 256, 0, st>>>(*a);
+            else if (ch == 16) k_compact_rows<16><<<grid, 256, 0, st>>>(*a);
+            else if (ch == 32) k_compact_rows<32><<<grid, 256, 0, st>>>(*a);
             else if (vec == 16) k_compact<16><<<grid, 256, 0, st>>>(*a);
             else if (vec == 8) k_compact<8><<<grid, 256, 0, st>>>(*a);
             else k_compact<4><<<grid, 256, 0, st>>>(*a);

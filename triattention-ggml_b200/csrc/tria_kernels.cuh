@@ -1551,6 +1551,51 @@ __global__ void __launch_bounds__(256) k_compact(const CompactArgs a) {
     }
 }
 
+/* Stable gather of rows of CH 16-byte chunks, CH dividing 32 (f16 rows of
+ * head_dim 64, 128, 256): CH lanes copy one row, so a warp moves 32 / CH rows
+ * per step, two steps' rows in flight, with one index load per row and no
+ * division. */
+template <int CH>
+__global__ void __launch_bounds__(256) k_compact_rows(const CompactArgs a) {
+    static_assert(32 % CH == 0, "rows per warp");
+    constexpr int RPW = 32 / CH;
+    const int u = blockIdx.y;
+    const int l = u / a.n_head_kv, h = u - l * a.n_head_kv;
+    const int nk = a.n_kept[u];
+    const int lane = threadIdx.x & 31, c = lane % CH, sub = lane / CH;
+    const int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
+    const uint8_t *ks = a.ks[l] + (int64_t)h * a.hs_s;
+    uint8_t *kd = a.kd[l] + (int64_t)h * a.hs_d;
+    const uint8_t *vs = a.has_v ? a.vs[l] + (int64_t)h * a.hs_s : nullptr;
+    uint8_t *vd = a.has_v ? a.vd[l] + (int64_t)h * a.hs_d : nullptr;
+    const int64_t wg = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t jb = wg * RPW * 2; jb < nk; jb += nw * RPW * 2) {
+        int jr[2], rr[2];
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            jr[q] = (int)(jb + q * RPW + sub);
+            rr[q] = jr[q] < nk ? kept[jr[q]] : 0;
+        }
+        uint4 kv[2], vv[2];
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            if (jr[q] >= nk) continue;
+            kv[q] = *reinterpret_cast<const uint4 *>(ks + (int64_t)rr[q] * a.cs_s + c * 16);
+            if (vs) vv[q] = *reinterpret_cast<const uint4 *>(vs + (int64_t)rr[q] * a.cs_s + c * 16);
+        }
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            if (jr[q] >= nk) continue;
+            *reinterpret_cast<uint4 *>(kd + (int64_t)jr[q] * a.cs_d + c * 16) = kv[q];
+            if (vs) *reinterpret_cast<uint4 *>(vd + (int64_t)jr[q] * a.cs_d + c * 16) = vv[q];
+            if (c == 0)
+                a.pos_d[(int64_t)u * a.cells_d + jr[q]] =
+                    a.pos_s[a.pos_shared_s ? (int64_t)rr[q] : (int64_t)u * a.cells_s + rr[q]];
+        }
+    }
+}
+
 /* Stable gather for rows that are 8 bytes off 16-byte alignment (q8_0 rows of
  * 136 bytes), when source and destination rows of a head share their
  * alignment modulo 16: each row moves as rb / 16 chunks of 16 bytes and one
