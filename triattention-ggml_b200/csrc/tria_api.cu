@@ -660,7 +660,7 @@ static int launch_compact(tria_ctx *c, const tria_kv_view *s, const tria_kv_view
     int vec = std::min({al(rb), al(s->cell_stride), al(s->head_stride), al(d->cell_stride), al(d->head_stride)});
     /* rows 8 bytes off 16-byte alignment whose source and destination share
      * that offset for every head: 16-byte chunks plus one 8-byte piece */
-    bool split = vec == 8 && rb % 16 == 8 && s->cell_stride % 16 == 0 && d->cell_stride % 16 == 0 &&
+    bool split = vec == 8 && rb % 16 == 8 && rb < 16 * 9 && s->cell_stride % 16 == 0 && d->cell_stride % 16 == 0 &&
                  (s->head_stride - d->head_stride) % 16 == 0;
     for (int l = 0; split && l < s->n_layer; l++) {
         auto a16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
@@ -701,6 +701,10 @@ static int launch_compact(tria_ctx *c, const tria_kv_view *s, const tria_kv_view
         const bool by_row = ch == 8 || ch == 16 || ch == 32;
         if (by_row) {   /* 256 threads move 2 * 256 / ch rows per step */
             grid.x = (unsigned)std::max<int64_t>(1, std::min<int64_t>(((int64_t)std::max(rows, 1) * ch + 511) / 512, 1024));
+        }
+        if (split) {    /* one destination cell (all kv heads) per warp, one block row per layer */
+            grid.x = (unsigned)std::max<int64_t>(1, std::min<int64_t>(((int64_t)std::max(rows, 1) + 7) / 8, 4096));
+            grid.y = (unsigned)nl;
         }
         if (max_rows > 0) {
             if (split) k_compact_split<<<grid, 256, 0, st>>>(*a);

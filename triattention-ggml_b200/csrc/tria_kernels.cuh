@@ -1598,38 +1598,42 @@ __global__ void __launch_bounds__(256) k_compact_rows(const CompactArgs a) {
 
 /* Stable gather for rows that are 8 bytes off 16-byte alignment (q8_0 rows of
  * 136 bytes), when source and destination rows of a head share their
- * alignment modulo 16: each row moves as rb / 16 chunks of 16 bytes and one
- * 8-byte piece (at the start of the row when the head's rows begin 8 bytes
- * off a 16-byte boundary, else at its end). */
+ * alignment modulo 16.  A row moves as rb / 16 (<= 8) chunks of 16 bytes plus
+ * one 8-byte piece (at the start of the row when the head's rows begin 8
+ * bytes off a 16-byte boundary, else at its end), 8 lanes a row.  A warp
+ * writes destination cell j of one layer for all its kv heads (4 heads a
+ * step): the heads' rows share 32-byte sectors, and writing a cell whole
+ * keeps those sectors from reaching memory piece by piece.  blockIdx.y is
+ * the layer. */
 __global__ void __launch_bounds__(256) k_compact_split(const CompactArgs a) {
-    const int u = blockIdx.y;
-    const int l = u / a.n_head_kv, h = u - l * a.n_head_kv;
-    const int nk = a.n_kept[u];
-    const int nseg = a.row_bytes / 16 + 1;
-    const bool lead8 = (((int64_t)h * a.hs_s) & 15) != 0;
-    const int64_t total = (int64_t)nk * nseg;
-    const int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
-    const uint8_t *ks = a.ks[l] + (int64_t)h * a.hs_s;
-    uint8_t *kd = a.kd[l] + (int64_t)h * a.hs_d;
-    const uint8_t *vs = a.has_v ? a.vs[l] + (int64_t)h * a.hs_s : nullptr;
-    uint8_t *vd = a.has_v ? a.vd[l] + (int64_t)h * a.hs_d : nullptr;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int jrow = (int)(i / nseg);
-        const int sg = (int)(i - (int64_t)jrow * nseg);
-        const int r = kept[jrow];
-        const int64_t so = (int64_t)r * a.cs_s, d0 = (int64_t)jrow * a.cs_d;
-        if (sg < nseg - 1) {
-            const int off = (lead8 ? 8 : 0) + 16 * sg;
-            *reinterpret_cast<uint4 *>(kd + d0 + off) = *reinterpret_cast<const uint4 *>(ks + so + off);
-            if (vs) *reinterpret_cast<uint4 *>(vd + d0 + off) = *reinterpret_cast<const uint4 *>(vs + so + off);
-        } else {
-            const int off = lead8 ? 0 : a.row_bytes - 8;
-            *reinterpret_cast<uint2 *>(kd + d0 + off) = *reinterpret_cast<const uint2 *>(ks + so + off);
-            if (vs) *reinterpret_cast<uint2 *>(vd + d0 + off) = *reinterpret_cast<const uint2 *>(vs + so + off);
+    const int l = blockIdx.y, KV = a.n_head_kv;
+    const int nch = a.row_bytes / 16;
+    const int lane = threadIdx.x & 31, c = lane & 7, sub = lane >> 3;
+    int nk_max = 0;
+    for (int h = 0; h < KV; h++) nk_max = max(nk_max, a.n_kept[l * KV + h]);
+    const int64_t wg = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t j = wg; j < nk_max; j += nw) {
+        const int jr = (int)j;
+        for (int h0 = 0; h0 < KV; h0 += 4) {
+            const int h = h0 + sub, u = l * KV + h;
+            if (h >= KV || jr >= a.n_kept[u]) continue;
+            const int r = a.kept_idx[(int64_t)u * a.kept_stride + jr];
+            const bool lead8 = (((int64_t)h * a.hs_s) & 15) != 0;
+            const int off16 = (lead8 ? 8 : 0) + 16 * c, off8 = lead8 ? 0 : a.row_bytes - 8;
+            const int64_t so = (int64_t)r * a.cs_s + (int64_t)h * a.hs_s, d0 = (int64_t)jr * a.cs_d + (int64_t)h * a.hs_d;
+            if (c < nch) {
+                *reinterpret_cast<uint4 *>(a.kd[l] + d0 + off16) = *reinterpret_cast<const uint4 *>(a.ks[l] + so + off16);
+                if (a.has_v)
+                    *reinterpret_cast<uint4 *>(a.vd[l] + d0 + off16) = *reinterpret_cast<const uint4 *>(a.vs[l] + so + off16);
+            }
+            if (c == 0) {
+                *reinterpret_cast<uint2 *>(a.kd[l] + d0 + off8) = *reinterpret_cast<const uint2 *>(a.ks[l] + so + off8);
+                if (a.has_v)
+                    *reinterpret_cast<uint2 *>(a.vd[l] + d0 + off8) = *reinterpret_cast<const uint2 *>(a.vs[l] + so + off8);
+                a.pos_d[(int64_t)u * a.cells_d + jr] = a.pos_s[a.pos_shared_s ? (int64_t)r : (int64_t)u * a.cells_s + r];
+            }
         }
-        if (sg == 0)
-            a.pos_d[(int64_t)u * a.cells_d + jrow] = a.pos_s[a.pos_shared_s ? (int64_t)r : (int64_t)u * a.cells_s + r];
     }
 }
 
