@@ -28,10 +28,12 @@
  *                  10-bit digits) of the keep-th largest key, ties to the
  *                  lowest rows, and warp ballots over contiguous row ranges
  *                  that write the kept row indices in order.
- *   k_compact      stable gather of kept K/V rows and positions into the
- *                  ping-pong buffer, vectorised, byte-exact.
+ *   k_compact_*    stable gather of kept K/V rows and positions into the
+ *                  ping-pong buffer, byte-exact: a lane group per f16 row,
+ *                  whole destination cells for q8_0 rows, vectors otherwise.
  *
- * No tensor cores: this is a streaming fp32 reduction bounded by HBM.
+ * No tensor cores: the scoring is a streaming fp32 reduction whose accuracy
+ * bar (1e-5 absolute on raw scores) a split-TF32 contraction misses.
  */
 #pragma once
 
