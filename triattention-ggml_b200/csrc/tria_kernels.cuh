@@ -403,6 +403,11 @@ __device__ __forceinline__ f2_t mul2(f2_t a, f2_t b) {
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+__device__ __forceinline__ f2_t add2(f2_t a, f2_t b) {
+    f2_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
 __device__ __forceinline__ f2_t sub2(f2_t a, f2_t b) {
     f2_t d;
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -905,15 +910,24 @@ __device__ __forceinline__ ZsRec zs_record(const ZsVals &xv, double approx) {
     const float scale = __int_as_float((150 - (exb - 127)) << 23);
     int lsum = 0, pl = 0x7fffffff, ph = -0x7fffffff - 1;
     bool special = false;
+    const f2_t sc2 = pk2(scale, scale), c2 = pk2(0x1.8p23f, 0x1.8p23f);
 #pragma unroll
-    for (int t = 0; t < ZS_EPL; t++) {
-        const float q = xs[t] * scale;
-        const float f = __fadd_rn(q, 0x1.8p23f);
-        const float fr = __fsub_rn(q, __fsub_rn(f, 0x1.8p23f));
-        special |= !(fabsf(q) < 0x1p22f) || fabsf(fr) == 0.5f;
-        lsum += (int)((uint32_t)__float_as_int(f) - 0x4b400000u);
-        pl = min(pl, lsum);
-        ph = max(ph, lsum);
+    for (int t = 0; t < ZS_EPL; t += 2) {
+        /* two elements per packed op; each op rounds as its scalar form */
+        const f2_t q2 = mul2(pk2(xs[t], xs[t + 1]), sc2);
+        const f2_t f2 = add2(q2, c2);
+        const f2_t fr2 = sub2(q2, sub2(f2, c2));
+        float q[2], f[2], fr[2];
+        upk(q2, q[0], q[1]);
+        upk(f2, f[0], f[1]);
+        upk(fr2, fr[0], fr[1]);
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            special |= !(fabsf(q[k]) < 0x1p22f) || fabsf(fr[k]) == 0.5f;
+            lsum += (int)((uint32_t)__float_as_int(f[k]) - 0x4b400000u);
+            pl = min(pl, lsum);
+            ph = max(ph, lsum);
+        }
     }
     if (__any_sync(0xffffffffu, special)) return zs_record_exact(xv, approx);
     int incl = lsum;
