@@ -10,10 +10,12 @@ positions into the ping-pong buffer.  Inputs are resident in HBM and larger
 than L2 (no flush needed).  Prints one JSON line on rank 0.
 
 Under torchrun (N > 1) every rank runs its own shard:
-  --scaling weak   (default) each rank evicts a full cache of the workload
-                   (per-GPU work fixed; e.g. one sequence per GPU);
-  --scaling strong the workload's kv heads are split across the ranks (total
-                   work fixed).
+  --scaling strong (default for N > 1) the workload's layers are partitioned
+                   into contiguous blocks, one per rank (36 layers over 8
+                   ranks: 5,5,5,5,4,4,4,4); total work fixed, no collective
+                   on the data path;
+  --scaling weak   each rank evicts a full cache of the workload (per-GPU
+                   work fixed; e.g. one sequence per GPU).
 The step is timed on the device with CUDA events and reported as the max over
 ranks.  `--impl reference` times the reference's CPU implementation
 (oracle/_ref = the reference's triattention.c, plus the oracle's select and
@@ -794,7 +796,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
+                    help="N > 1: strong (default) = layers partitioned over the ranks; weak = a full cache per rank")
     ap.add_argument("--layers", type=int, default=0,
                     help="profile a smaller case: only the first N layers of the workload")
     ap.add_argument("--no-e2e", action="store_true")
@@ -803,6 +806,8 @@ def main():
                     help="time the 5-step exponential ramp schedule (10/20/40/80/100%%, +128 rows between steps)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.scaling is None:
+        args.scaling = "strong" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "weak"
     if args.layers:
         CONFIGS[args.config] = dict(CONFIGS[args.config], L=args.layers)
     if args.impl == "reference":

@@ -112,7 +112,8 @@ enum tria_status {
     TRIA_ERR_NOMEM       = -3,  /* device allocation failed */
     TRIA_ERR_POSITION    = -4,  /* a key position lies outside [0, cur_pos] */
     TRIA_ERR_UNSUPPORTED = -5,  /* geometry or cache type not supported */
-    TRIA_ERR_NO_DEVICE   = -6   /* no CUDA device / not an sm_100 device */
+    TRIA_ERR_NO_DEVICE   = -6,  /* no CUDA device / not an sm_100 device */
+    TRIA_ERR_TIMEOUT     = -7   /* a bounded wait inside a kernel gave up; that step's output is undefined */
 };
 
 /* Cache element types (ggml type ids). */
@@ -255,6 +256,23 @@ TRIA_API int tria_ctx_stage_ms(tria_ctx *ctx, float *ms, int cap);
 /* Number of kernels this context has launched so far. */
 TRIA_API int64_t tria_ctx_launches(const tria_ctx *ctx);
 
+/* Status of the kernels this context ran since the last check, for callers
+ * that run tria_score / tria_select / tria_compact themselves (tria_evict
+ * reports it through tria_get_n_kv): synchronises `stream`, returns TRIA_OK,
+ * TRIA_ERR_POSITION (a key position outside [0, cur_pos]) or TRIA_ERR_TIMEOUT
+ * (a pipeline wait of the scoring kernel gave up), and clears the status.
+ * New; the reference has no error path (triattention.c:198 returns void). */
+TRIA_API int tria_ctx_check(tria_ctx *ctx, void *stream);
+
+/* Fault-injection hook for tests of the timeout path: every pipeline wait of
+ * the scoring kernel (TMA stages, partial buffers, position ring) gives up
+ * after `cycles` SM clock cycles instead of about a second, sets the
+ * timeout status and lets the kernel return; copies already issued are
+ * still waited for with the default bound before a block exits.  cycles <= 0
+ * restores the default.  A step that timed out reports TRIA_ERR_TIMEOUT from
+ * tria_get_n_kv / tria_ctx_check and leaves the context usable. */
+TRIA_API int tria_ctx_set_wait_limit(tria_ctx *ctx, int64_t cycles);
+
 /* Device-pointer form of tria_score_kv_head for one (layer, kv-head):
  * k_re/k_im [n][fc] fp32, key_pos [n] int32, out [n] fp32, all device. */
 TRIA_API int tria_score_kv_head_dev(tria_ctx *ctx, const float *k_re, const float *k_im,
@@ -264,6 +282,8 @@ TRIA_API int tria_score_kv_head_dev(tria_ctx *ctx, const float *k_re, const floa
 /* Maximum number of scores tria_select_noalloc can rank in one call
  * (sum over units of the per-unit row capacity, see below): 1 Mi keys, 4 MiB. */
 #define TRIA_NOALLOC_MAX_KEYS (1 << 20)
+/* Maximum number of (layer, kv-head) units in one tria_select_noalloc call. */
+#define TRIA_NOALLOC_MAX_UNITS 2048
 
 /* Selection that allocates no memory at all.  No counterpart in the
  * reference: it exists for callers that must not allocate device memory at
@@ -279,13 +299,17 @@ TRIA_API int tria_score_kv_head_dev(tria_ctx *ctx, const float *k_re, const floa
  *   n_rows    host, [units] rows per unit (each <= score_stride, kept_stride)
  *   keep      host, [units] rows to keep (clamped to [protected rows, n_rows])
  *   pos       device positions, [units][pos_stride] or one shared [rows] array
- *             when pos_stride == 0; may be NULL when window == sink == 0
+ *             when pos_stride == 0 (0 <= pos_stride <= INT32_MAX); may be
+ *             NULL when window == sink == 0
  *   kept_idx  device, [units][kept_stride] kept row indices, ascending
  *   n_kept    device, [units] kept counts
+ * 1 <= units <= TRIA_NOALLOC_MAX_UNITS (TRIA_ERR_INVALID otherwise), and
  * units * (max n_rows rounded up to 64) must not exceed TRIA_NOALLOC_MAX_KEYS
  * (TRIA_ERR_UNSUPPORTED otherwise, nothing launched).  Runs on the current
  * device; the first call on a device looks the array's address up
  * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * The address is kept for the life of the process: do not call this again
+ * on a device after resetting it (cudaDeviceReset).
  * All calls share the one array: calls that overlap on the GPU (different
  * streams, or different host threads) race and corrupt each other's result. */
 TRIA_API int tria_select_noalloc(const float *scores, int64_t score_stride,

@@ -15,18 +15,33 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libtria_ref.so")
-REF_SRC = os.environ.get("TRIA_REF_SRC", "/root/reference")
+REF_SRC = os.environ.get("TRIA_REF_SRC", "")      # the reference source tree, when it is present
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
 
 
-def build(ref: bool = True) -> None:
-    """Compile liboracle.so, and _ref/ when the reference sources are present."""
+def build(ref: bool = True, ref_src: str = "") -> None:
+    """Compile liboracle.so, and _ref/ when the reference sources are given
+    (ref_src, else the environment variable TRIA_REF_SRC) and present."""
     subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
-    if ref and os.path.isdir(REF_SRC) and os.path.exists(os.path.join(REF_SRC, "triattention.c")):
-        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={REF_SRC}"], check=True)
+    src = ref_src or REF_SRC
+    if ref and src and os.path.exists(os.path.join(src, "triattention.c")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={src}"], check=True)
+        if os.path.exists(os.path.join(os.path.dirname(HERE), "triattention-ggml_b200", "libtriattention_b200.so")):
+            subprocess.run(["make", "-s", "-C", HERE, "dropin", f"REF={src}"], check=True)
+
+
+def dropin_tool(name: str) -> str:
+    """Path of a reference C driver (test_tria_gqa, test_tria_lib, bench_tria)
+    compiled unmodified against the product header and library."""
+    return os.path.join(HERE, "_ref", "dropin_" + name)
+
+
+def ref_tool(name: str) -> str:
+    """Path of a reference C driver compiled against the reference itself."""
+    return os.path.join(HERE, "_ref", name)
 
 
 class OracleUnit(C.Structure):

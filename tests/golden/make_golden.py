@@ -1,8 +1,9 @@
 #!/usr/bin/env python3
 """Regenerate the committed golden fixtures from the reference itself.
 
-Needs the reference tree (REF, default /root/reference) and the compiled
-reference library (`make -C oracle ref`).  Outputs, all under tests/golden/:
+Needs the reference source tree, given as the first argument or in the
+environment variable TRIA_REF_SRC (there is no default), and the compiled
+reference library (`make -C oracle ref REF=<reference tree>`).  Outputs, all under tests/golden/:
 
   synth_l2h8kv4.tria          seeded TRIA v2 stats (2 layers, 8 heads, 4 kv, hd 128,
                               theta 1e6, layer scales 0.9 / 1.1)
@@ -16,7 +17,7 @@ reference library (`make -C oracle ref`).  Outputs, all under tests/golden/:
                               i32 fc, n, cur_pos, layer, kv_head; i32 key_pos[n];
                               f32 k_re[n*fc]; f32 k_im[n*fc]; f32 expected[n]
 
-Run:  python tests/golden/make_golden.py [REF]
+Run:  python tests/golden/make_golden.py <reference tree>
 """
 import ctypes
 import os
@@ -30,7 +31,10 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(REPO, "triattention-ggml_b200"))
 import workloads  # noqa: E402
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TRIA_REF_SRC", "")
+if not REF or not os.path.exists(os.path.join(REF, "triattention.c")):
+    sys.exit("make_golden.py: give the reference source tree (the directory holding triattention.c) "
+             "as the first argument or in TRIA_REF_SRC")
 
 
 def run_exporter(script, stats, out, layer, head):

@@ -143,3 +143,24 @@ def test_no_gpu_fails_loudly(synth_stats_path):
         assert np.isnan(out).all()
     finally:
         tria_b200.free(st)
+
+
+def test_select_noalloc_rejects_bad_sizes_on_the_host(L):
+    """Argument checks of tria_select_noalloc run before any CUDA call (no
+    device needed, nothing launched): a negative or over-int32 position
+    stride and a unit count above TRIA_NOALLOC_MAX_UNITS are refused."""
+    units, n = 4, 100
+    nr = np.full(units, n, np.int32)
+    keep = np.full(units, 10, np.int32)
+    fake = 256                                   # never dereferenced: the checks fail first
+    for stride in (-1, 1 << 31):
+        r = L.tria_select_noalloc(fake, n, nr.ctypes.data, keep.ctypes.data, units, fake, stride, n, 8, 0,
+                                  fake, n, fake, None)
+        assert r == tria_b200.ERR_INVALID, stride
+        assert "pos_stride" in tria_b200.last_error()
+    big = 2049
+    nr2 = np.full(big, 1, np.int32)
+    keep2 = np.ones(big, np.int32)
+    r = L.tria_select_noalloc(fake, 1, nr2.ctypes.data, keep2.ctypes.data, big, None, 0, 1, 0, 0,
+                              fake, 1, fake, None)
+    assert r == tria_b200.ERR_INVALID and "units" in tria_b200.last_error()

@@ -69,6 +69,31 @@ def test_noalloc_matches_tria_select_twice(synth_stats_path):
             ka, kb = kept.cpu().numpy(), kept_ref.cpu().numpy()
             for u in range(L * KV):
                 assert np.array_equal(ka[u, :nk_a[u]], kb[u, :nk_b[u]]), (n_cells, u)
+        # one shared [rows] position array (pos_stride == 0), window and sink on,
+        # against tria_select on a view whose positions are shared
+        n_cells = 4000
+        scores, n_rows = _case(rng, L, KV, n_cells, True)
+        cur = n_cells + 3
+        shared = np.sort(rng.choice(cur, n_cells, replace=False)).astype(np.int32)
+        view_cache = devcache.DeviceCache(workloads.TYPE_F16, L, KV, hd, n_cells, dev, with_v=False)
+        view_cache.fill_from_host(np.zeros((L, n_cells, KV * 2 * hd), np.uint8), None, None, shared)
+        params = tria_b200.EvictParams(cur, 500, 100, 300, 8, 0)
+        d_scores = torch.from_numpy(scores).to(dev)
+        kept_ref = torch.full((L * KV, n_cells), -1, dtype=torch.int32, device=dev)
+        nk_ref = torch.zeros(L * KV, dtype=torch.int32, device=dev)
+        ctx.select(view_cache.view(shared_pos=True), n_rows, d_scores, params, kept_ref, nk_ref)
+        keep = np.array([workloads.layer_keep(int(n_rows[u]), workloads.layer_budget(scales[u // KV], 500), 100)
+                         for u in range(L * KV)], np.int32)
+        kept = torch.full((L * KV, n_cells), -1, dtype=torch.int32, device=dev)
+        nk = torch.zeros(L * KV, dtype=torch.int32, device=dev)
+        tria_b200.select_noalloc(d_scores, n_cells, n_rows, keep, kept, n_cells, nk,
+                                 pos=view_cache.pos_shared, pos_stride=0, cur_pos=cur, window=300, sink=8)
+        torch.cuda.synchronize()
+        nk_a, nk_b = nk.cpu().numpy(), nk_ref.cpu().numpy()
+        assert np.array_equal(nk_a, nk_b)
+        ka, kb = kept.cpu().numpy(), kept_ref.cpu().numpy()
+        for u in range(L * KV):
+            assert np.array_equal(ka[u, :nk_a[u]], kb[u, :nk_b[u]]), ("shared", u)
     finally:
         ctx.close()
         tria_b200.free(st)

@@ -48,6 +48,7 @@ extern "C" TRIA_API const char *tria_status_str(int st) {
         case TRIA_ERR_POSITION: return "key position outside [0, cur_pos]";
         case TRIA_ERR_UNSUPPORTED: return "unsupported geometry";
         case TRIA_ERR_NO_DEVICE: return "no sm_100 CUDA device";
+        case TRIA_ERR_TIMEOUT: return "a bounded wait inside a kernel gave up";
         default: return "unknown status";
     }
 }
@@ -65,6 +66,21 @@ struct DeviceGuard {
     }
     ~DeviceGuard() { if (prev >= 0) cudaSetDevice(prev); }
 };
+
+/* The status word the kernels set (ST_* bits) as a tria_status, with the
+ * message of the first bit found.  A pipeline timeout is reported before a
+ * position error: a step that timed out left raw scores unwritten, whatever
+ * else it saw. */
+static int status_of_bits(int32_t bits, const char *what) {
+    if (bits == 0) return TRIA_OK;
+    if (bits & ST_TIMEOUT)
+        FAIL(TRIA_ERR_TIMEOUT, "%s: a pipeline wait of the scoring kernel gave up (status 0x%x); "
+             "that step's output is undefined", what, bits);
+    if (bits & ST_POSITION)
+        FAIL(TRIA_ERR_POSITION, "%s: a key position was outside [0, cur_pos] (status 0x%x); "
+             "that step's output is undefined", what, bits);
+    FAIL(TRIA_ERR_CUDA, "%s: unknown kernel status bits 0x%x", what, bits);
+}
 
 /* ------------------------------------------------------------------ */
 /* Context                                                              */
@@ -99,7 +115,8 @@ struct tria_ctx {
     size_t io_cap = 0;
     cudaStream_t own_stream = nullptr;
     /* status / counts read-back */
-    int32_t *d_status = nullptr;
+    int32_t *d_status = nullptr;         /* ST_* bits the kernels set; cleared when read back */
+    long long wait_limit = WAIT_LIMIT_DEFAULT;   /* bound of the scoring kernel's pipeline waits */
     int32_t *h_pinned = nullptr;         /* [0] = status, [1..] counts */
     int32_t pinned_cap = 0;
     int32_t last_units = 0;
@@ -543,6 +560,7 @@ static int launch_score_ws(tria_ctx *c, const tria_kv_view *v, const int32_t *n_
     a->raw = c->raw + (int64_t)l0 * KV * c->G * c->raw_stride;
     a->raw_stride = c->raw_stride;
     a->status = c->d_status;
+    a->wait_limit = c->wait_limit;
     a->tiles_per_layer = (max_rows + plan.tile - 1) / plan.tile;
     a->n_items = a->tiles_per_layer * nl;
     int rc = TRIA_OK;
@@ -879,10 +897,11 @@ extern "C" TRIA_API int tria_get_n_kv(tria_ctx *c, int32_t *n_kept, int32_t cap)
     if (!c->have_step) return 0;
     DeviceGuard g(c->device);
     CUDA_TRY(cudaEventSynchronize(c->ev_done));
-    if (c->h_pinned[0] & ST_POSITION) {
+    if (c->h_pinned[0]) {
+        const int32_t bits = c->h_pinned[0];
         cudaMemset(c->d_status, 0, 4);
         c->h_pinned[0] = 0;
-        FAIL(TRIA_ERR_POSITION, "a key position was outside [0, cur_pos]; that step's output is undefined");
+        return status_of_bits(bits, "tria_get_n_kv");
     }
     int mx = 0;
     for (int u = 0; u < c->last_units; u++) {
@@ -1197,6 +1216,25 @@ extern "C" TRIA_API int tria_ctx_stage_ms(tria_ctx *c, float *ms, int cap) {
 
 extern "C" TRIA_API int64_t tria_ctx_launches(const tria_ctx *c) { return c ? c->launches : -1; }
 
+extern "C" TRIA_API int tria_ctx_check(tria_ctx *c, void *stream) {
+    if (!c) FAIL(TRIA_ERR_INVALID, "tria_ctx_check: null ctx");
+    DeviceGuard g(c->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    int32_t bits = 0;
+    CUDA_TRY(cudaMemcpyAsync(&bits, c->d_status, 4, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    if (!bits) return TRIA_OK;
+    CUDA_TRY(cudaMemsetAsync(c->d_status, 0, 4, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    return status_of_bits(bits, "tria_ctx_check");
+}
+
+extern "C" TRIA_API int tria_ctx_set_wait_limit(tria_ctx *c, int64_t cycles) {
+    if (!c) FAIL(TRIA_ERR_INVALID, "tria_ctx_set_wait_limit: null ctx");
+    c->wait_limit = cycles > 0 ? (long long)cycles : WAIT_LIMIT_DEFAULT;
+    return TRIA_OK;
+}
+
 /* Score one (layer, kv-head) from fp32 split halves in device memory; the
  * delta range [dlo, dhi] must already be covered by the table. */
 static int score_split(tria_ctx *c, const float *k_re, const float *k_im, const int32_t *pos, int32_t cur_pos,
@@ -1357,7 +1395,7 @@ static int score_host(tria_ctx *c, const float *k_re, const float *k_im, const i
     CUDA_TRY(cudaStreamSynchronize(st));
     if (status) {
         cudaMemset(c->d_status, 0, 4);
-        FAIL(TRIA_ERR_POSITION, "delta outside the table");
+        return status_of_bits(status, "tria_score_kv_head");
     }
     return TRIA_OK;
 }
@@ -1394,7 +1432,10 @@ extern "C" TRIA_API void tria_score_kv_head(const tria_stats *stats, const float
 static __device__ __align__(256) uint32_t g_noalloc_keys[TRIA_NOALLOC_MAX_KEYS];
 
 static std::mutex g_noalloc_mu;
-static uint32_t *g_noalloc_ptr[256];   /* device address of g_noalloc_keys, per device */
+/* Device address of g_noalloc_keys, per device, looked up once.  A device
+ * reset (cudaDeviceReset) unloads the module and makes it stale: a process
+ * that resets a device must not call tria_select_noalloc on it again. */
+static uint32_t *g_noalloc_ptr[256];
 
 /* Device address of the static key array on the current device, looked up
  * once per device (host code cannot use the symbol itself as a pointer). */
@@ -1421,10 +1462,12 @@ extern "C" TRIA_API int tria_select_noalloc(const float *scores, int64_t score_s
                                             void *stream) {
     if (!scores || !n_rows || !keep || !kept_idx || !n_kept)
         FAIL(TRIA_ERR_INVALID, "tria_select_noalloc: null argument");
-    if (units < 1 || units > TRIA_MAX_UNITS)
-        FAIL(TRIA_ERR_INVALID, "tria_select_noalloc: units %d outside [1, %d]", units, TRIA_MAX_UNITS);
+    if (units < 1 || units > TRIA_NOALLOC_MAX_UNITS)
+        FAIL(TRIA_ERR_INVALID, "tria_select_noalloc: units %d outside [1, %d]", units, TRIA_NOALLOC_MAX_UNITS);
     if ((window > 0 || sink > 0) && !pos)
         FAIL(TRIA_ERR_INVALID, "tria_select_noalloc: window/sink need positions");
+    if (pos && (pos_stride < 0 || pos_stride > INT32_MAX))
+        FAIL(TRIA_ERR_INVALID, "tria_select_noalloc: pos_stride %lld outside [0, %d]", (long long)pos_stride, INT32_MAX);
     int32_t max_rows = 0;
     for (int u = 0; u < units; u++) {
         if (n_rows[u] < 0 || n_rows[u] > score_stride || n_rows[u] > kept_stride ||

@@ -8,6 +8,9 @@
 #define TRIA_MAX_GQA        16      /* query heads per kv head */
 #define TRIA_MAX_LAYERS     128     /* layers per kernel launch (views are split above) */
 #define TRIA_MAX_UNITS      2048    /* (layer, kv-head) units per kernel launch */
+#if TRIA_MAX_UNITS != TRIA_NOALLOC_MAX_UNITS
+#error "tria_select_noalloc ranks one launch of units"
+#endif
 
 #ifdef __cplusplus
 extern "C" {

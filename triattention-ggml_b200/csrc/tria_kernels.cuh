@@ -47,7 +47,10 @@
 namespace tria {
 
 enum : int { KT_F32SPLIT = 0, KT_F16 = TRIA_TYPE_F16, KT_Q8_0 = TRIA_TYPE_Q8_0 };
-enum : int { ST_POSITION = 1 };
+/* Bits of the device status word (tria_ctx's d_status), decoded on the host
+ * by tria_status_of_bits(): a key position outside the table, a bounded
+ * pipeline wait that gave up. */
+enum : int { ST_POSITION = 1, ST_TIMEOUT = 2 };
 
 constexpr int N_OFF = 17;
 constexpr int SCORE_THREADS = 256;
@@ -281,7 +284,6 @@ __global__ void __launch_bounds__(SCORE_THREADS) k_score_raw(const ScoreArgs a) 
 /* contiguous: llama.cpp's layout), head_dim 128                        */
 /* ------------------------------------------------------------------ */
 
-constexpr int ST_TIMEOUT = 2;          /* status bit: a pipeline wait gave up */
 constexpr int WS_TILE_MAX = 32;        /* cells per work item: 32, or 16 when 32 does not fit */
 constexpr int WS_CWARPS = 8;           /* consumer warps: one kv head each */
 constexpr int WS_THREADS = (WS_CWARPS + 4) * 32;   /* + a producer warpgroup, one warp of it working */
@@ -313,6 +315,7 @@ struct TmaScoreArgs {
     float *raw;
     int64_t raw_stride;
     int32_t *status;
+    long long wait_limit;                 /* cycles a pipeline wait may take before it gives up (ST_TIMEOUT) */
     int32_t tiles_per_layer, n_items;
     int32_t layer_rows[TRIA_MAX_LAYERS];  /* max rows over the layer's heads */
     int32_t n_rows[TRIA_MAX_UNITS];
@@ -375,12 +378,14 @@ __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
                  "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
     return ok != 0;
 }
-/* Wait for a phase of `bar`, giving up after ~2^31 cycles (about a second). */
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+/* Default bound of a pipeline wait: ~2^31 cycles, about a second. */
+constexpr long long WAIT_LIMIT_DEFAULT = 1ll << 31;
+/* Wait for a phase of `bar`, giving up after `limit` cycles. */
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long long limit = WAIT_LIMIT_DEFAULT) {
     if (mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try(bar, parity))
-        if (clock64() - t0 > (1ll << 31)) return false;
+        if (clock64() - t0 > limit) return false;
     return true;
 }
 
@@ -545,7 +550,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         for (int k = 0; k < n_mine; k++) {
             const int c0 = t * SC_T;
             const int cells = max(0, min(SC_T, a.layer_rows[l] - c0));
-            if (!mbar_wait(&full[st], phase)) {
+            if (!mbar_wait(&full[st], phase, a.wait_limit)) {
                 if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
                 s_abort = 1;
             }
@@ -642,7 +647,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);           /* the stage is no longer read */
             /* partial sums -> buffer pk once the reducers are done with its previous item */
-            if (!mbar_wait(&pfree[pk], pph ^ 1u)) {
+            if (!mbar_wait(&pfree[pk], pph ^ 1u, a.wait_limit)) {
                 if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
                 s_abort = 1;
             }
@@ -705,8 +710,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         for (; k < n_mine && !s_abort; k++) {
             const int st = k % S;
             if (pos_issued < n_mine) fetch_pos(pos_issued++);   /* ring slot of item k-1: done with */
-            if (!mbar_wait(&posbar[k % WS_POS_RING], (uint32_t)((k / WS_POS_RING) & 1)) ||
-                !mbar_wait(&empty[st], (uint32_t)(((k / S) & 1) ^ 1))) {
+            if (!mbar_wait(&posbar[k % WS_POS_RING], (uint32_t)((k / WS_POS_RING) & 1), a.wait_limit) ||
+                !mbar_wait(&empty[st], (uint32_t)(((k / S) & 1) ^ 1), a.wait_limit)) {
                 if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
                 s_abort = 1;
                 break;
@@ -761,12 +766,17 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
             __syncwarp();
             if (lane == 0) mbar_arrive(&full[st]);       /* also publishes the slot stores */
         }
-        /* drain: every copy issued must land before the CTA exits */
+        /* drain: every copy issued must land before the CTA exits.  These
+         * waits keep the default bound whatever a.wait_limit says: the copies
+         * always complete, and a shortened limit (the timeout-path test) must
+         * not let the CTA exit with a copy still writing its shared memory. */
         if (lane == 0) {
+            bool ok = true;
             for (int kk = max(0, k - S); kk < k; kk++)
-                mbar_wait(&full[kk % S], (uint32_t)((kk / S) & 1));
+                ok &= mbar_wait(&full[kk % S], (uint32_t)((kk / S) & 1));
             for (int kk = k; kk < pos_issued; kk++)
-                mbar_wait(&posbar[kk % WS_POS_RING], (uint32_t)((kk / WS_POS_RING) & 1));
+                ok &= mbar_wait(&posbar[kk % WS_POS_RING], (uint32_t)((kk / WS_POS_RING) & 1));
+            if (!ok) atomicOr(a.status, ST_TIMEOUT);
         }
         return;
     }
@@ -781,7 +791,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         int pk = 0;
         uint32_t pph = 0;
         for (int k = 0; k < n_mine; k++) {
-            if (!mbar_wait(&pfull[pk], pph)) {
+            if (!mbar_wait(&pfull[pk], pph, a.wait_limit)) {
                 if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
                 s_abort = 1;
             }

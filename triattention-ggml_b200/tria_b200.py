@@ -36,6 +36,7 @@ ERR_NOMEM = -3
 ERR_POSITION = -4
 ERR_UNSUPPORTED = -5
 ERR_NO_DEVICE = -6
+ERR_TIMEOUT = -7
 
 
 class TriaError(RuntimeError):
@@ -141,6 +142,8 @@ def lib() -> C.CDLL:
         L.tria_ctx_stage_ms.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
         L.tria_ctx_launches.restype = C.c_int64
         L.tria_ctx_launches.argtypes = [C.c_void_p]
+        L.tria_ctx_check.argtypes = [C.c_void_p, C.c_void_p]
+        L.tria_ctx_set_wait_limit.argtypes = [C.c_void_p, C.c_int64]
         L.tria_select_noalloc.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int32,
                                           C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
                                           C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]
@@ -364,6 +367,15 @@ class Context:
 
     def launches(self) -> int:
         return int(lib().tria_ctx_launches(self.h))
+
+    def check(self, stream=None):
+        """tria_ctx_check: raise TriaError if a kernel of this context reported a
+        bad position or a pipeline timeout since the last check."""
+        check(lib().tria_ctx_check(self.h, _stream(stream)))
+
+    def set_wait_limit(self, cycles: int = 0):
+        """tria_ctx_set_wait_limit (timeout-path tests): 0 restores the default."""
+        check(lib().tria_ctx_set_wait_limit(self.h, int(cycles)))
 
     def score_kv_head_dev(self, k_re, k_im, key_pos, cur_pos, n, layer, kv_head, out, stream=None):
         check(lib().tria_score_kv_head_dev(self.h, _ptr(k_re), _ptr(k_im), _ptr(key_pos), int(cur_pos),
