@@ -389,6 +389,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long l
     return true;
 }
 
+/* One warp's pipeline wait on a phase of `bar`.  The outcome is made the same
+ * in every lane (a lane that saw the phase complete still gives up when
+ * another lane timed out), so a warp leaves its loop as a whole and never
+ * reaches a full-mask shuffle or __syncwarp with lanes missing.  On a timeout
+ * lane 0 records ST_TIMEOUT and raises the block's abort flag; a warp also
+ * gives up when another warp of the block raised it.  The bound is read (from
+ * shared memory) only when the first try fails, so it occupies no register in
+ * the math loops.  Returns true to go on. */
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, const volatile long long *limit,
+                                          volatile int *abort_flag, int32_t *status) {
+    bool done = mbar_try(bar, parity);
+    if (!done) done = mbar_wait(bar, parity, *limit);
+    const bool ok = __all_sync(0xffffffffu, done);
+    if (!ok && (threadIdx.x & 31) == 0) {
+        atomicOr(status, ST_TIMEOUT);
+        *abort_flag = 1;
+    }
+    return !__any_sync(0xffffffffu, !ok || *abort_flag != 0);
+}
+
 typedef unsigned long long f2_t;          /* two packed fp32 for the f32x2 instructions */
 __device__ __forceinline__ f2_t pk2(float a, float b) {
     f2_t r;
@@ -505,6 +525,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
     uint64_t *pfree = pfull + plan.part_slots;           /* partials of an item reduced */
     const int P = plan.part_slots, LP = plan.lp();
     __shared__ volatile int s_abort;
+    __shared__ volatile long long s_wait_limit;         /* a.wait_limit, read on slow waits only */
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
@@ -512,6 +533,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         for (int i = 0; i < WS_POS_RING; i++) mbar_init(&posbar[i], 1);
         for (int i = 0; i < P; i++) { mbar_init(&pfull[i], WS_CWARPS); mbar_init(&pfree[i], WS_RWARPS); }
         s_abort = 0;
+        s_wait_limit = a.wait_limit;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -550,11 +572,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         for (int k = 0; k < n_mine; k++) {
             const int c0 = t * SC_T;
             const int cells = max(0, min(SC_T, a.layer_rows[l] - c0));
-            if (!mbar_wait(&full[st], phase, a.wait_limit)) {
-                if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
-                s_abort = 1;
-            }
-            if (s_abort) break;
+            if (!warp_wait(&full[st], phase, &s_wait_limit, &s_abort, a.status)) break;
             const uint8_t *sb = stages + st * stage_bytes;
             const uint8_t *tab = sb + plan.k_bytes();
             const int32_t *slot = reinterpret_cast<const int32_t *>(tab + plan.tab_bytes(FC));
@@ -647,11 +665,12 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);           /* the stage is no longer read */
             /* partial sums -> buffer pk once the reducers are done with its previous item */
-            if (!mbar_wait(&pfree[pk], pph ^ 1u, a.wait_limit)) {
-                if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
-                s_abort = 1;
+            /* (a lighter uniform form than warp_wait: the G accumulators are live here;
+             * another warp's abort is seen at the next stage wait) */
+            if (__any_sync(0xffffffffu, !mbar_wait(&pfree[pk], pph ^ 1u, s_wait_limit))) {
+                if (lane == 0) { atomicOr(a.status, ST_TIMEOUT); s_abort = 1; }
+                break;
             }
-            if (s_abort) break;
             if (cb < cend) {
                 float *pb = part + pk * plan.part_floats();
 #pragma unroll
@@ -707,15 +726,13 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         int pos_issued = 0;                              /* items whose positions were requested */
         for (; pos_issued < min(WS_POS_RING - 1, n_mine); pos_issued++) fetch_pos(pos_issued);
         int k = 0;
-        for (; k < n_mine && !s_abort; k++) {
+        for (; k < n_mine; k++) {
+            if (__any_sync(0xffffffffu, s_abort != 0)) break;
             const int st = k % S;
             if (pos_issued < n_mine) fetch_pos(pos_issued++);   /* ring slot of item k-1: done with */
-            if (!mbar_wait(&posbar[k % WS_POS_RING], (uint32_t)((k / WS_POS_RING) & 1), a.wait_limit) ||
-                !mbar_wait(&empty[st], (uint32_t)(((k / S) & 1) ^ 1), a.wait_limit)) {
-                if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
-                s_abort = 1;
+            if (!warp_wait(&posbar[k % WS_POS_RING], (uint32_t)((k / WS_POS_RING) & 1), &s_wait_limit, &s_abort, a.status) ||
+                !warp_wait(&empty[st], (uint32_t)(((k / S) & 1) ^ 1), &s_wait_limit, &s_abort, a.status))
                 break;
-            }
             /* the consumers' reads of this stage happen before these async writes */
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             int l, c0;
@@ -791,11 +808,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         int pk = 0;
         uint32_t pph = 0;
         for (int k = 0; k < n_mine; k++) {
-            if (!mbar_wait(&pfull[pk], pph, a.wait_limit)) {
-                if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
-                s_abort = 1;
-            }
-            if (s_abort) break;
+            if (!warp_wait(&pfull[pk], pph, &s_wait_limit, &s_abort, a.status)) break;
             const int c0 = t * SC_T;
             const int cells = max(0, min(SC_T, a.layer_rows[l] - c0));
             const float *pb = part + pk * plan.part_floats();
