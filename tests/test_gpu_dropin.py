@@ -38,6 +38,9 @@ def test_reference_bench_runs_on_product(torch_dev, tmp_path):
     stats = workloads.write_tria(str(tmp_path / "b.tria"), 4, 32, 8, 128, seed=3)
     r = subprocess.run([exe, stats], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
-    rows = [ln.split() for ln in r.stdout.splitlines() if ln.strip() and ln.split()[0].isdigit()]
+    def timing_row(ln):                 # "seq_len time_ms us/head", three numbers
+        t = ln.split()
+        return len(t) == 3 and t[0].isdigit() and all(x.replace(".", "", 1).isdigit() for x in t[1:])
+    rows = [ln.split() for ln in r.stdout.splitlines() if timing_row(ln)]
     assert [int(x[0]) for x in rows] == [256, 512, 1024, 2048, 4096], r.stdout
     assert "tria_score_kv_head:" not in r.stderr, r.stderr      # no failure message from the library

@@ -378,10 +378,27 @@ __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
                  "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
     return ok != 0;
 }
+/* Non-blocking test of a phase (test_wait never suspends the thread). */
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
 /* Default bound of a pipeline wait: ~2^31 cycles, about a second. */
 constexpr long long WAIT_LIMIT_DEFAULT = 1ll << 31;
-/* Wait for a phase of `bar`, giving up after `limit` cycles. */
+/* Wait for a phase of `bar`, giving up after `limit` cycles.  try_wait may
+ * suspend the thread until the phase completes, which is the cheap way to
+ * wait but can outlast a short bound; a bound shortened below the default
+ * (the timeout-path test hook) polls with test_wait instead, so it is
+ * checked every few dozen cycles. */
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long long limit = WAIT_LIMIT_DEFAULT) {
+    if (limit < WAIT_LIMIT_DEFAULT) {
+        const long long t0 = clock64();
+        while (!mbar_test(bar, parity))
+            if (clock64() - t0 > limit) return false;
+        return true;
+    }
     if (mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try(bar, parity))
@@ -394,14 +411,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long l
  * another lane timed out), so a warp leaves its loop as a whole and never
  * reaches a full-mask shuffle or __syncwarp with lanes missing.  On a timeout
  * lane 0 records ST_TIMEOUT and raises the block's abort flag; a warp also
- * gives up when another warp of the block raised it.  The bound is read (from
- * shared memory) only when the first try fails, so it occupies no register in
- * the math loops.  Returns true to go on. */
+ * gives up when another warp of the block raised it.  The bound is read from
+ * shared memory at each wait, so it occupies no register in the math loops.
+ * Returns true to go on. */
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, const volatile long long *limit,
                                           volatile int *abort_flag, int32_t *status) {
-    bool done = mbar_try(bar, parity);
-    if (!done) done = mbar_wait(bar, parity, *limit);
-    const bool ok = __all_sync(0xffffffffu, done);
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, parity, *limit));
     if (!ok && (threadIdx.x & 31) == 0) {
         atomicOr(status, ST_TIMEOUT);
         *abort_flag = 1;
