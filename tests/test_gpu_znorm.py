@@ -50,9 +50,13 @@ def _same(a, b):
     return (a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))
 
 
-def test_znorm_stats_bit_exact(oracle):
+@pytest.mark.parametrize("copies", [1, 9])
+def test_znorm_stats_bit_exact(oracle, copies):
+    """copies=1: few chains (the whole-pass kernel); copies=9: 306 chains,
+    more than two per SM (the window-by-window kernel)."""
     import torch
-    chains = _chains()
+    base = _chains()
+    chains = {f"{k}#{i}": v for i in range(copies) for k, v in base.items()}
     names = list(chains)
     stride = (max(x.size for x in chains.values()) + 63) // 64 * 64
     host = np.full((len(names), stride), np.nan, np.float32)

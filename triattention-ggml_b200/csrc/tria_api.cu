@@ -431,6 +431,34 @@ static void fill_score_args(const tria_ctx *c, const tria_kv_view *v, const int3
     }
 }
 
+/* The z-norm statistics of z.units * z.G chains.  Both kernels are exact;
+ * they differ in latency and throughput (measured on B200, 32768-element
+ * chains): k_znorm_pre (records of a whole pass at once, 8 warps a chain)
+ * finishes a chain sooner when few chains share the GPU (128 chains: 66 us
+ * against 76 us), k_znorm_seg (window by window, 4 warps a chain, 8 chains an
+ * SM) keeps more chains going at once and wins from a few chains per SM on
+ * (1152 chains: 136 us against 160-190 us).  k_znorm_pre also needs the
+ * longest chain to fit its shared-memory plan. */
+static cudaError_t launch_znorm_chains(const ZArgs &z, int chains, int sm_count, cudaStream_t st) {
+    if (chains <= 0) return cudaSuccess;
+    int n_max = 0;
+    for (int u = 0; u < z.units; u++) n_max = std::max(n_max, z.n_rows[u]);
+    const int nseg = (n_max + ZS_SEG - 1) / ZS_SEG;
+    if (nseg > ZP_MAX_SEG || chains > 2 * sm_count) {
+        k_znorm_seg<<<chains, ZS_WARPS * 32, 0, st>>>(z);
+        return cudaGetLastError();
+    }
+    static bool attr_set = false;          /* the opt-in maximum, once per process (per device is not needed: same limit) */
+    if (!attr_set) {
+        const cudaError_t e = cudaFuncSetAttribute(k_znorm_pre, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   zp_smem_bytes(ZP_MAX_SEG));
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    k_znorm_pre<<<chains, ZP_WARPS * 32, zp_smem_bytes(nseg), st>>>(z);
+    return cudaGetLastError();
+}
+
 static int launch_znorm(tria_ctx *c, int64_t unit0, int units, const int32_t *n_rows, cudaStream_t st) {
     ZArgs z;
     z.raw = c->raw + unit0 * c->G * c->raw_stride;
@@ -439,9 +467,7 @@ static int launch_znorm(tria_ctx *c, int64_t unit0, int units, const int32_t *n_
     z.units = units;
     z.ms = c->ms + unit0 * c->G;
     for (int u = 0; u < units; u++) z.n_rows[u] = n_rows[unit0 + u];
-    const int chains = units * (int)c->G;
-    if (chains > 0) k_znorm_seg<<<chains, ZS_WARPS * 32, 0, st>>>(z);
-    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(launch_znorm_chains(z, units * (int)c->G, c->sm_count, st));
     c->launches++;
     return TRIA_OK;
 }
@@ -659,9 +685,30 @@ static int launch_select(tria_ctx *c, const tria_kv_view *v, const int32_t *n_ro
             a->n_rows[u] = n_rows[u0 + u];
             a->keep_req[u] = keep[u0 + u];
         }
-        if (fused) k_select<true><<<units, SELECT_BLOCK, 0, st>>>(*a);
-        else k_select<false><<<units, SELECT_BLOCK, 0, st>>>(*a);
+        int n_max = 0;
+        for (int u = 0; u < units; u++) n_max = std::max(n_max, a->n_rows[u]);
+        cudaError_t e = cudaSuccess;
+        if (n_max <= SELECT_SMEM_KEYS) {       /* the unit's keys in shared memory */
+            static bool attr_set = false;
+            if (!attr_set) {
+                const size_t mx = (size_t)SELECT_SMEM_KEYS * 4;
+                e = cudaFuncSetAttribute(k_select<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mx);
+                if (e == cudaSuccess)
+                    e = cudaFuncSetAttribute(k_select<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mx);
+                attr_set = e == cudaSuccess;
+            }
+            const size_t smem = (size_t)std::max(n_max, 1) * 4;
+            if (e == cudaSuccess) {
+                if (fused) k_select<true, true><<<units, SELECT_BLOCK_SM, smem, st>>>(*a);
+                else k_select<false, true><<<units, SELECT_BLOCK_SM, smem, st>>>(*a);
+            }
+        } else if (fused) {
+            k_select<true, false><<<units, SELECT_BLOCK, 0, st>>>(*a);
+        } else {
+            k_select<false, false><<<units, SELECT_BLOCK, 0, st>>>(*a);
+        }
         delete a;
+        if (e != cudaSuccess) FAIL(TRIA_ERR_CUDA, "k_select: %s", cudaGetErrorString(e));
         CUDA_TRY(cudaGetLastError());
         c->launches++;
         return TRIA_OK;
@@ -926,8 +973,9 @@ extern "C" TRIA_API int tria_znorm_stats(const float *x, int64_t stride, const i
         z.units = cn;
         z.ms = reinterpret_cast<float2 *>(mean_std) + c0;
         for (int i = 0; i < cn; i++) z.n_rows[i] = n[c0 + i];
-        if (cn > 0) k_znorm_seg<<<cn, ZS_WARPS * 32, 0, (cudaStream_t)stream>>>(z);
-        CUDA_TRY(cudaGetLastError());
+        int dev = 0, sms = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        CUDA_TRY(launch_znorm_chains(z, cn, sms, (cudaStream_t)stream));
     }
     return TRIA_OK;
 }
@@ -1502,7 +1550,7 @@ extern "C" TRIA_API int tria_select_noalloc(const float *scores, int64_t score_s
         a.n_rows[u] = n_rows[u];
         a.keep_req[u] = keep[u];
     }
-    k_select<false><<<units, SELECT_BLOCK, 0, (cudaStream_t)stream>>>(a);
+    k_select<false, false><<<units, SELECT_BLOCK, 0, (cudaStream_t)stream>>>(a);
     CUDA_TRY(cudaGetLastError());
     return TRIA_OK;
 }

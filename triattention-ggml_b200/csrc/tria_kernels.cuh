@@ -1065,10 +1065,12 @@ __device__ __forceinline__ float zs_serial(const float *v, int cnt, float s) {
     return __shfl_sync(0xffffffffu, acc, 0);
 }
 
-/* Warp 0: advance s over the window's records s_rec[0..cnt) (<= 32); the
- * window's values are staged in s_vals (ZS_SEG per segment), `n_last` of
- * them live in the last segment. */
-__device__ __forceinline__ float zs_walk(const ZsRec *s_rec, int cnt, const float *s_vals, int n_last, float s) {
+/* One warp: advance s over the records s_rec[0..cnt) (<= 32).  A record that
+ * cannot be taken whole (ties beyond two, a binade crossing, a start in
+ * another binade than its guess, special values) is added element by element
+ * by slow(i, s), which returns the sum after record i's elements. */
+template <class Slow>
+__device__ __forceinline__ float zs_walk_cb(const ZsRec *s_rec, int cnt, float s, Slow slow) {
     const int lane = threadIdx.x & 31;
     ZsRec r = lane < cnt ? s_rec[lane] : ZsRec{ZS_SLOW, 0, 0, 0};
     int cur = 0;
@@ -1116,11 +1118,20 @@ __device__ __forceinline__ float zs_walk(const ZsRec *s_rec, int cnt, const floa
             const int m2 = M + delta + a1 + a2;
             s = __uint_as_float((bits & 0x80000000u) | ((uint32_t)exb << 23) | ((uint32_t)(m2 * sg) & 0x7fffffu));
         } else {
-            s = zs_serial(s_vals + cur * ZS_SEG, cur == cnt - 1 ? n_last : ZS_SEG, s);
+            s = slow(cur, s);
         }
         cur++;
     }
     return s;
+}
+
+/* Warp 0: advance s over the window's records s_rec[0..cnt) (<= 32); the
+ * window's values are staged in s_vals (ZS_SEG per segment), `n_last` of
+ * them live in the last segment. */
+__device__ __forceinline__ float zs_walk(const ZsRec *s_rec, int cnt, const float *s_vals, int n_last, float s) {
+    return zs_walk_cb(s_rec, cnt, s, [&](int cur, float v) {
+        return zs_serial(s_vals + cur * ZS_SEG, cur == cnt - 1 ? n_last : ZS_SEG, v);
+    });
 }
 
 /* One pass of a chain: the sequential fp32 sum of val(x[0..n)).  All threads
@@ -1211,6 +1222,242 @@ __global__ void __launch_bounds__(ZS_WARPS * 32, 8) k_znorm_seg(const ZArgs a) {
         return __fmul_rn(d, d);
     }, s_sum, s_rec, s_vals, &s_state);
     if (threadIdx.x == 0) {
+        float sd = __fsqrt_rn(__fdiv_rn(var, (float)n));
+        if (sd < 1e-6f) sd = 1e-6f;
+        a.ms[t] = make_float2(mean, sd);
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* Z-norm statistics, records of a whole pass at once                   */
+/* ------------------------------------------------------------------ */
+/*
+ * The same exact chains as k_znorm_seg, with the latency taken out of them.
+ * k_znorm_seg guesses each window's binades from the exact sum at the window
+ * start, so every window waits for the walk of the one before.  Here a first
+ * sweep takes, per segment of ZS_SEG elements, sums of x - c and (x - c)^2
+ * (c = x[0]; fp32 is plenty for a guess); a scan in double turns them into an
+ * approximate chain value at every segment start, for the first pass, and --
+ * once the exact mean m is known -- for the second (sum of (x - m)^2 =
+ * s2 - 2 d s1 + len d^2, d = m - c).  Every segment's record is then computed
+ * in one parallel sweep, and one warp walks them all.  A guess only decides
+ * which records the walk can take whole: a wrong one sends that segment
+ * through the plain fp32 adds, so the result is the reference's chain bit
+ * for bit whatever the guesses.  The sweeps stage the values of segments
+ * likely to need plain adds (a record flagged slow, or a guessed binade
+ * change within the segment) in shared memory, so the walk rarely waits on
+ * a global load.  Per chain this is three reads of the chain (sums, pass 1,
+ * pass 2) and two walks; all of a pass's records are independent.
+ */
+constexpr int ZP_WARPS = 8;
+constexpr int ZP_SLOTS = 12;                  /* staged segments per pass */
+constexpr int ZP_MAX_SEG = 6144;              /* segments (x ZS_SEG elements) the shared plan holds */
+
+/* Dynamic shared memory of k_znorm_pre for chains of up to nseg segments. */
+__host__ __device__ __forceinline__ int zp_smem_bytes(int nseg) {
+    return nseg * (int)sizeof(ZsRec) + nseg * 12 + ((nseg * 2 + 15) & ~15) + (ZP_SLOTS + 1) * ZS_SEG * 4;
+}
+
+/* This lane's ZS_EPL consecutive elements of segment `seg`, val() applied to
+ * live ones, 0 past n (x 16-byte aligned; rows padded to a multiple of 4). */
+template <class Val>
+__device__ __forceinline__ void zp_load(const float *x, int n, int seg, Val val, ZsVals &xs) {
+    const int e0 = seg * ZS_SEG + ZS_EPL * (threadIdx.x & 31);
+#pragma unroll
+    for (int v4 = 0; v4 < ZS_EPL; v4 += 4) {
+        const int e = e0 + v4;
+        const int live = max(0, min(4, n - e));
+        float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (live > 0) w = *reinterpret_cast<const float4 *>(x + e);
+        xs.v[v4 + 0] = live > 0 ? val(w.x) : 0.f;
+        xs.v[v4 + 1] = live > 1 ? val(w.y) : 0.f;
+        xs.v[v4 + 2] = live > 2 ? val(w.z) : 0.f;
+        xs.v[v4 + 3] = live > 3 ? val(w.w) : 0.f;
+    }
+}
+
+/* Every warp's segments warp, warp + ZP_WARPS, ... in batches of ZP_BATCH:
+ * the batch's loads are all issued first (ZP_BATCH x 32 bytes in flight per
+ * lane), then body(seg, xs) runs on each with val() applied to the live
+ * elements and 0 elsewhere. */
+constexpr int ZP_BATCH = 4;
+template <class Val, class Body>
+__device__ __forceinline__ void zp_sweep(const float *x, int n, int nseg, Val val, Body body) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int s0 = warp; s0 < nseg; s0 += ZP_BATCH * ZP_WARPS) {
+        float4 w[ZP_BATCH][ZS_EPL / 4];
+#pragma unroll
+        for (int b = 0; b < ZP_BATCH; b++) {
+            const int e0 = (s0 + b * ZP_WARPS) * ZS_SEG + ZS_EPL * lane;
+#pragma unroll
+            for (int v4 = 0; v4 < ZS_EPL / 4; v4++) {
+                const int e = e0 + 4 * v4;
+                w[b][v4] = e < n ? *reinterpret_cast<const float4 *>(x + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < ZP_BATCH; b++) {
+            const int seg = s0 + b * ZP_WARPS;
+            if (seg >= nseg) break;                     /* warp-uniform */
+            const int e0 = seg * ZS_SEG + ZS_EPL * lane;
+            ZsVals xs;
+#pragma unroll
+            for (int v4 = 0; v4 < ZS_EPL / 4; v4++) {
+                const float4 q = w[b][v4];
+                const int e = e0 + 4 * v4;
+                xs.v[4 * v4 + 0] = e + 0 < n ? val(q.x) : 0.f;
+                xs.v[4 * v4 + 1] = e + 1 < n ? val(q.y) : 0.f;
+                xs.v[4 * v4 + 2] = e + 2 < n ? val(q.z) : 0.f;
+                xs.v[4 * v4 + 3] = e + 3 < n ? val(q.w) : 0.f;
+            }
+            body(seg, xs);
+        }
+    }
+}
+
+/* One warp: ap[j] = (float)(exclusive prefix of f over segments < j), in double;
+ * returns the total. */
+template <class F>
+__device__ __forceinline__ double zp_scan(int nseg, F f, float *ap) {
+    const int lane = threadIdx.x & 31;
+    double carry = 0.0;
+    for (int b = 0; b < nseg; b += 32) {
+        const int j = b + lane;
+        const double v = j < nseg ? f(j) : 0.0;
+        double incl = v;
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) {
+            const double y = __shfl_up_sync(0xffffffffu, incl, m);
+            if (lane >= m) incl += y;
+        }
+        if (j < nseg) ap[j] = (float)(carry + (incl - v));
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    return carry;
+}
+
+struct ZpSmem {
+    ZsRec *rec;            /* [nseg] records of the current pass */
+    float *s1, *s2, *ap;   /* [nseg] shifted sums; approximate chain value at each segment start */
+    int16_t *slot;         /* [nseg] staging slot of a segment, -1 none */
+    float *stage;          /* [ZP_SLOTS][ZS_SEG] staged values */
+    float *wbuf;           /* [ZS_SEG] the walk's own buffer for unstaged segments */
+};
+
+__device__ __forceinline__ int zp_exp(float v) { return (int)((__float_as_uint(v) >> 23) & 0xff); }
+
+/* One pass: the sequential fp32 sum of val(x[0..n)), every thread gets it. */
+template <class Val>
+__device__ float zp_pass(const float *x, int n, int nseg, Val val, const ZpSmem &S, int *s_nst, float *s_state) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) *s_nst = 0;
+    __syncthreads();
+    zp_sweep(x, n, nseg, val, [&](int seg, const ZsVals &xs) {
+        const float a0 = S.ap[seg];
+        const ZsRec r = zs_record(xs, (double)a0);
+        /* likely plain adds: a slow record, or the guessed value changes binade */
+        const bool pred = (r.f & ZS_SLOW) || (seg + 1 < nseg && zp_exp(S.ap[seg + 1]) != zp_exp(a0));
+        int sl = -1;
+        if (lane == 0) {
+            S.rec[seg] = r;
+            if (pred) {
+                const int k = atomicAdd(s_nst, 1);
+                if (k < ZP_SLOTS) sl = k;
+            }
+            S.slot[seg] = (int16_t)sl;
+        }
+        sl = __shfl_sync(0xffffffffu, sl, 0);
+        if (sl >= 0) {
+            float *d = S.stage + sl * ZS_SEG + ZS_EPL * lane;
+#pragma unroll
+            for (int v4 = 0; v4 < ZS_EPL; v4 += 4)
+                *reinterpret_cast<float4 *>(d + v4) = make_float4(xs.v[v4], xs.v[v4 + 1], xs.v[v4 + 2], xs.v[v4 + 3]);
+        }
+    });
+    __syncthreads();
+    if (warp == 0) {
+        float s = 0.f;
+        for (int b = 0; b < nseg; b += 32) {
+            s = zs_walk_cb(S.rec + b, min(32, nseg - b), s, [&](int cur, float v) -> float {
+                const int seg = b + cur;
+                const int cnt = seg == nseg - 1 ? n - seg * ZS_SEG : ZS_SEG;
+                const int sl = S.slot[seg];
+                const float *src = S.wbuf;
+                if (sl >= 0) {
+                    src = S.stage + sl * ZS_SEG;
+                } else {
+                    ZsVals xs;
+                    zp_load(x, n, seg, val, xs);
+                    float *d = S.wbuf + ZS_EPL * lane;
+#pragma unroll
+                    for (int v4 = 0; v4 < ZS_EPL; v4 += 4)
+                        *reinterpret_cast<float4 *>(d + v4) = make_float4(xs.v[v4], xs.v[v4 + 1], xs.v[v4 + 2], xs.v[v4 + 3]);
+                    __syncwarp();
+                }
+                const float out = zs_serial(src, cnt, v);
+                __syncwarp();                        /* wbuf is free again */
+                return out;
+            });
+        }
+        if (lane == 0) *s_state = s;
+    }
+    __syncthreads();
+    const float s = *s_state;
+    __syncthreads();
+    return s;
+}
+
+/* One CTA per chain: (mean, std) of triattention.c:227-238, chains of up to
+ * ZP_MAX_SEG * ZS_SEG elements. */
+__global__ void __launch_bounds__(ZP_WARPS * 32) k_znorm_pre(const ZArgs a) {
+    extern __shared__ __align__(16) uint8_t zsm[];
+    __shared__ int s_nst;
+    __shared__ float s_state;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int t = blockIdx.x;
+    const int n = a.n_rows[t / a.G];
+    const float *x = a.raw + (int64_t)t * a.raw_stride;
+    const int nseg = (n + ZS_SEG - 1) / ZS_SEG;
+    ZpSmem S;                                          /* 16-byte pieces first: staging, records */
+    S.stage = reinterpret_cast<float *>(zsm);
+    S.wbuf = S.stage + ZP_SLOTS * ZS_SEG;
+    S.rec = reinterpret_cast<ZsRec *>(S.wbuf + ZS_SEG);
+    S.s1 = reinterpret_cast<float *>(S.rec + nseg);
+    S.s2 = S.s1 + nseg;
+    S.ap = S.s2 + nseg;
+    S.slot = reinterpret_cast<int16_t *>(S.ap + nseg);
+
+    /* per segment: sums of x - c and (x - c)^2, c = x[0] (near the data, so
+     * fp32 is plenty for a guess) */
+    const float c = n > 0 ? x[0] : 0.f;
+    zp_sweep(x, n, nseg, [c](float v) { return v - c; }, [&](int seg, const ZsVals &xs) {
+        float a1 = 0.f, a2 = 0.f;
+#pragma unroll
+        for (int q = 0; q < ZS_EPL; q++) {
+            a1 += xs.v[q];
+            a2 = fmaf(xs.v[q], xs.v[q], a2);
+        }
+#pragma unroll
+        for (int m = 16; m; m >>= 1) {
+            a1 += __shfl_xor_sync(0xffffffffu, a1, m);
+            a2 += __shfl_xor_sync(0xffffffffu, a2, m);
+        }
+        if (lane == 0) { S.s1[seg] = a1; S.s2[seg] = a2; }
+    });
+    __syncthreads();
+    auto len = [&](int j) { return (double)min(ZS_SEG, n - j * ZS_SEG); };
+    if (warp == 0) zp_scan(nseg, [&](int j) { return (double)S.s1[j] + (double)c * len(j); }, S.ap);
+    const float sum = zp_pass(x, n, nseg, [](float v) { return v; }, S, &s_nst, &s_state);
+    const float mean = __fdiv_rn(sum, (float)n);
+    if (warp == 0) {
+        const double d = (double)mean - (double)c;
+        zp_scan(nseg, [&](int j) { return (double)S.s2[j] - 2.0 * d * (double)S.s1[j] + len(j) * d * d; }, S.ap);
+    }
+    const float var = zp_pass(x, n, nseg, [mean](float v) {
+        const float d = __fsub_rn(v, mean);
+        return __fmul_rn(d, d);
+    }, S, &s_nst, &s_state);
+    if (tid == 0) {
         float sd = __fsqrt_rn(__fdiv_rn(var, (float)n));
         if (sd < 1e-6f) sd = 1e-6f;
         a.ms[t] = make_float2(mean, sd);
@@ -1360,20 +1607,23 @@ __device__ __forceinline__ int ordered_keep(int n, uint32_t T, int allow, int32_
     return gt_all + min(eq_all, al);
 }
 
+/* Keys of up to SELECT_SMEM_KEYS rows fit in a k_select<*, true> block's
+ * shared memory (with the 16 KB histogram): one block per SM, 1024 threads. */
+constexpr int SELECT_SMEM_KEYS = 48 * 1024;
+constexpr int SELECT_BLOCK_SM = 1024;
+
+/* Selection of unit u by the whole block: keys (in `keys`, shared or global
+ * memory), radix select, ordered output.  FUSED: keys from the raw scores and
+ * the (mean, std) of the unit's query heads in s_zs (shared); else from
+ * a.scores.  s_hist is the block's [4096] histogram. */
 template <bool FUSED>
-__global__ void __launch_bounds__(SELECT_BLOCK, 2) k_select(const SelectArgs a) {
-    __shared__ int s_hist[4096];
-    __shared__ int s_warp[32];
-    __shared__ int s_bc[2];
-    const int u = blockIdx.x, tid = threadIdx.x, bd = blockDim.x;
+__device__ __forceinline__ void select_unit(const SelectArgs &a, int u, uint32_t *keys, const float2 *s_zs,
+                                            int *s_hist, int *s_warp, int *s_bc) {
+    const int tid = threadIdx.x, bd = blockDim.x;
     const int n = a.n_rows[u];
-    uint32_t *keys = a.keys + (int64_t)u * a.key_stride;
     int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
     const bool prot_on = a.window > 0 || a.sink > 0;
-
-    /* (mean, std) of the unit's query heads */
-    __shared__ float2 s_zs[TRIA_MAX_GQA];
-    if (FUSED && tid < a.G) s_zs[tid] = a.ms[(int64_t)u * a.G + tid];
+    for (int i = tid; i < 4096; i += bd) s_hist[i] = 0;
     __syncthreads();
     /* keys, SB rows per thread in flight (the raw scores are L2 / DRAM round
      * trips).  Fused: two 16-byte loads of 4 consecutive rows per query head
@@ -1422,6 +1672,7 @@ __global__ void __launch_bounds__(SELECT_BLOCK, 2) k_select(const SelectArgs a) 
                 prot++;
             }
             keys[r] = k;
+            atomicAdd(&s_hist[k >> 20], 1);              /* the first digit's histogram */
         }
     }
     const int n_prot = prot_on ? block_sum(prot, s_warp) : 0;
@@ -1448,18 +1699,20 @@ __global__ void __launch_bounds__(SELECT_BLOCK, 2) k_select(const SelectArgs a) 
         const int shift = pass == 0 ? 20 : (pass == 1 ? 10 : 0);
         const int nb = pass == 0 ? 4096 : 1024;
         const int hi = shift + 10;                       /* bits above this digit (pass > 0) */
-        for (int i = tid; i < nb; i += bd) s_hist[i] = 0;
-        __syncthreads();
-        for (int rb = tid; rb < n; rb += 8 * bd) {
-            uint32_t kk[8];
+        if (pass > 0) {                                  /* pass 0's histogram came with the keys */
+            for (int i = tid; i < nb; i += bd) s_hist[i] = 0;
+            __syncthreads();
+            for (int rb = tid; rb < n; rb += 8 * bd) {
+                uint32_t kk[8];
 #pragma unroll
-            for (int j = 0; j < 8; j++) kk[j] = rb + j * bd < n ? keys[rb + j * bd] : 0u;
+                for (int j = 0; j < 8; j++) kk[j] = rb + j * bd < n ? keys[rb + j * bd] : 0u;
 #pragma unroll
-            for (int j = 0; j < 8; j++)
-                if (rb + j * bd < n && (pass == 0 || (kk[j] >> hi) == (prefix >> hi)))
-                    atomicAdd(&s_hist[(kk[j] >> shift) & (uint32_t)(nb - 1)], 1);
+                for (int j = 0; j < 8; j++)
+                    if (rb + j * bd < n && (kk[j] >> hi) == (prefix >> hi))
+                        atomicAdd(&s_hist[(kk[j] >> shift) & (uint32_t)(nb - 1)], 1);
+            }
+            __syncthreads();
         }
-        __syncthreads();
         /* thread t owns bins [t*c, t*c + c); count of keys in bins >= its first */
         const int c = (nb + bd - 1) / bd;
         int own = 0;
@@ -1482,6 +1735,22 @@ __global__ void __launch_bounds__(SELECT_BLOCK, 2) k_select(const SelectArgs a) 
     /* keys above the threshold, and the first `need` equal to it in row order */
     const int kept_n = ordered_keep(n, prefix, need, kept, [&](int r) { return keys[r]; });
     if (tid == 0) a.n_kept[u] = kept_n;
+}
+
+/* SMK: the unit's keys live in dynamic shared memory (n <= SELECT_SMEM_KEYS),
+ * so the radix passes and the ordered output never leave the SM; else in
+ * a.keys (global).  Either way the first digit's histogram is built in the
+ * key pass. */
+template <bool FUSED, bool SMK>
+__global__ void __launch_bounds__(SMK ? SELECT_BLOCK_SM : SELECT_BLOCK, SMK ? 1 : 2) k_select(const SelectArgs a) {
+    __shared__ int s_hist[4096];
+    __shared__ int s_warp[32];
+    __shared__ int s_bc[2];
+    __shared__ float2 s_zs[TRIA_MAX_GQA];           /* (mean, std) of the unit's query heads */
+    extern __shared__ __align__(16) uint32_t s_keys[];
+    const int u = blockIdx.x;
+    if (FUSED && (int)threadIdx.x < a.G) s_zs[threadIdx.x] = a.ms[(int64_t)u * a.G + threadIdx.x];
+    select_unit<FUSED>(a, u, SMK ? s_keys : a.keys + (int64_t)u * a.key_stride, s_zs, s_hist, s_warp, s_bc);
 }
 
 /* ------------------------------------------------------------------ */
