@@ -142,3 +142,75 @@ def test_global_select_two_gloo_ranks():
         assert len(got) == len(exp)
         for a, b in zip(got, exp):
             assert a == b.tolist()
+
+
+def _dead_rank_main(rank, world, port, q, mode, dead):
+    """One global-budget step on every rank, then rank `dead` leaves (exits,
+    or stalls without joining the next step); the others run a second step
+    and must get an error from their next gather, not hang."""
+    import time
+    from datetime import timedelta
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=4))
+    rng = np.random.default_rng(5)
+    all_seqs = [_make_seq_keys(rng, 12, 1, 200, False) for _ in range(2)]
+    per = 12 // world
+    mine = [{"keys": keys[rank * per:(rank + 1) * per]} for keys in all_seqs]
+
+    def gather(t):
+        out = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(out, t.contiguous())
+        return torch.stack(out)
+
+    gb.global_select(mine, [50, 500], gather, CpuBackend(), rank)          # step 1: every rank
+    def report(*msg):                          # flush before os._exit, which skips the queue's feeder
+        q.put(msg)
+        q.close()
+        q.join_thread()
+
+    if rank == dead:
+        report(rank, "left", 0.0)
+        if mode == "stall":
+            time.sleep(60)                                                  # never joins step 2
+        os._exit(0)
+    t0 = time.monotonic()
+    try:
+        gb.global_select(mine, [50, 500], gather, CpuBackend(), rank)      # step 2: a peer is gone
+        report(rank, "no error", time.monotonic() - t0)
+    except Exception as e:                                                  # noqa: BLE001
+        report(rank, "error: " + type(e).__name__, time.monotonic() - t0)
+    os._exit(0)                                # no destroy_process_group with a peer gone
+
+
+@pytest.mark.parametrize("mode", ["exit", "stall"])
+def test_global_select_dead_rank_fails_fast(mode):
+    """Failure detection on the collective path: a rank that exits or stops
+    between steps makes every other rank's next step raise within the process
+    group's timeout (4 s here) instead of waiting forever."""
+    import time
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world, dead = 3, 2
+    procs = [ctx.Process(target=_dead_rank_main, args=(r, world, port, q, mode, dead)) for r in range(world)]
+    t0 = time.monotonic()
+    for p in procs:
+        p.start()
+    try:
+        res = sorted(q.get(timeout=90) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=5)
+            if p.is_alive():
+                p.kill()
+                p.join()
+    assert res[dead][1] == "left"
+    for r in range(world):
+        if r == dead:
+            continue
+        assert res[r][1].startswith("error"), res
+        assert res[r][2] < 30.0, res                     # bounded by the group timeout, not a hang
+    assert time.monotonic() - t0 < 120

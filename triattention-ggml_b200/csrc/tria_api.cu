@@ -508,10 +508,11 @@ static WsPlan ws_plan(const tria_ctx *c, const tria_kv_view *v) {
 }
 
 template <int KT, int G, int T, bool DT = false>
-static int launch_ws_inst(const TmaScoreArgs &a, const WsPlan &plan, int grid, cudaStream_t st) {
-    auto fn = k_score_ws<KT, G, T, DT>;
+static int launch_ws_inst(const TmaScoreArgs &a, const WsPlan &plan, int grid, cudaStream_t st, bool tw) {
+    auto fn = tw ? k_score_ws<KT, G, T, DT, true> : k_score_ws<KT, G, T, DT, false>;
     /* the setmaxnreg split inside the kernel assumes this launch allocation */
-    static int regs = -1;
+    static int regs_of[2] = {-1, -1};
+    int &regs = regs_of[tw ? 1 : 0];
     if (regs < 0) {
         cudaFuncAttributes fa;
         CUDA_TRY(cudaFuncGetAttributes(&fa, fn));
@@ -528,24 +529,24 @@ static int launch_ws_inst(const TmaScoreArgs &a, const WsPlan &plan, int grid, c
 }
 
 template <int KT>
-static int launch_ws_g(int G, const TmaScoreArgs &a, const WsPlan &plan, int grid, cudaStream_t st) {
+static int launch_ws_g(int G, const TmaScoreArgs &a, const WsPlan &plan, int grid, cudaStream_t st, bool tw) {
     const bool t32 = plan.tile == 32;
     if (plan.direct) {
         switch (G) {
-            case 1: return launch_ws_inst<KT, 1, 16, true>(a, plan, grid, st);
-            case 2: return launch_ws_inst<KT, 2, 16, true>(a, plan, grid, st);
-            case 4: return launch_ws_inst<KT, 4, 16, true>(a, plan, grid, st);
-            case 5: return launch_ws_inst<KT, 5, 16, true>(a, plan, grid, st);
-            case 6: return launch_ws_inst<KT, 6, 16, true>(a, plan, grid, st);
+            case 1: return launch_ws_inst<KT, 1, 16, true>(a, plan, grid, st, tw);
+            case 2: return launch_ws_inst<KT, 2, 16, true>(a, plan, grid, st, tw);
+            case 4: return launch_ws_inst<KT, 4, 16, true>(a, plan, grid, st, tw);
+            case 5: return launch_ws_inst<KT, 5, 16, true>(a, plan, grid, st, tw);
+            case 6: return launch_ws_inst<KT, 6, 16, true>(a, plan, grid, st, tw);
             default: FAIL(TRIA_ERR_UNSUPPORTED, "k_score_ws: gqa %d not instantiated", G);
         }
     }
     switch (G) {
-        case 1: return t32 ? launch_ws_inst<KT, 1, 32>(a, plan, grid, st) : launch_ws_inst<KT, 1, 16>(a, plan, grid, st);
-        case 2: return t32 ? launch_ws_inst<KT, 2, 32>(a, plan, grid, st) : launch_ws_inst<KT, 2, 16>(a, plan, grid, st);
-        case 4: return t32 ? launch_ws_inst<KT, 4, 32>(a, plan, grid, st) : launch_ws_inst<KT, 4, 16>(a, plan, grid, st);
-        case 5: return launch_ws_inst<KT, 5, 16>(a, plan, grid, st);
-        case 6: return launch_ws_inst<KT, 6, 16>(a, plan, grid, st);
+        case 1: return t32 ? launch_ws_inst<KT, 1, 32>(a, plan, grid, st, tw) : launch_ws_inst<KT, 1, 16>(a, plan, grid, st, tw);
+        case 2: return t32 ? launch_ws_inst<KT, 2, 32>(a, plan, grid, st, tw) : launch_ws_inst<KT, 2, 16>(a, plan, grid, st, tw);
+        case 4: return t32 ? launch_ws_inst<KT, 4, 32>(a, plan, grid, st, tw) : launch_ws_inst<KT, 4, 16>(a, plan, grid, st, tw);
+        case 5: return launch_ws_inst<KT, 5, 16>(a, plan, grid, st, tw);
+        case 6: return launch_ws_inst<KT, 6, 16>(a, plan, grid, st, tw);
         default: FAIL(TRIA_ERR_UNSUPPORTED, "k_score_ws: gqa %d not instantiated", G);
     }
 }
@@ -592,8 +593,9 @@ static int launch_score_ws(tria_ctx *c, const tria_kv_view *v, const int32_t *n_
     int rc = TRIA_OK;
     if (a->n_items > 0) {
         const int grid = std::min(a->n_items, c->sm_count);
-        rc = v->type == TRIA_TYPE_F16 ? launch_ws_g<KT_F16>((int)c->G, *a, plan, grid, st)
-                                      : launch_ws_g<KT_Q8_0>((int)c->G, *a, plan, grid, st);
+        const bool tw = c->wait_limit != WAIT_LIMIT_DEFAULT;       /* the timeout-test instantiation */
+        rc = v->type == TRIA_TYPE_F16 ? launch_ws_g<KT_F16>((int)c->G, *a, plan, grid, st, tw)
+                                      : launch_ws_g<KT_Q8_0>((int)c->G, *a, plan, grid, st, tw);
         if (!rc) c->launches++;
     }
     delete a;

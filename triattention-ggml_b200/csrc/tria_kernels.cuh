@@ -406,6 +406,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long l
     return true;
 }
 
+/* mbar_wait with the bound in shared memory, read only when the first try
+ * fails (the common case is one try_wait). */
+__device__ __forceinline__ bool mbar_wait_first(uint64_t *bar, uint32_t parity, const volatile long long *limit) {
+    if (mbar_try(bar, parity)) return true;
+    return mbar_wait(bar, parity, *limit);
+}
+
+/* warp_wait without the abort flag, for waits where registers are scarce:
+ * true (in every lane) when the phase completed within the bound. */
+__device__ __forceinline__ bool warp_wait_light(uint64_t *bar, uint32_t parity, const volatile long long *limit) {
+    return __all_sync(0xffffffffu, mbar_wait_first(bar, parity, limit));
+}
+
 /* One warp's pipeline wait on a phase of `bar`.  The outcome is made the same
  * in every lane (a lane that saw the phase complete still gives up when
  * another lane timed out), so a warp leaves its loop as a whole and never
@@ -416,7 +429,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long l
  * Returns true to go on. */
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, const volatile long long *limit,
                                           volatile int *abort_flag, int32_t *status) {
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, parity, *limit));
+    const bool ok = __all_sync(0xffffffffu, mbar_wait_first(bar, parity, limit));
     if (!ok && (threadIdx.x & 31) == 0) {
         atomicOr(status, ST_TIMEOUT);
         *abort_flag = 1;
@@ -518,9 +531,13 @@ __device__ __forceinline__ f2_t q8_pair(const uint4 &w, int i) {
  * The producer warpgroup runs on WS_PRODUCER_REGS
  * registers and hands the rest to the consumers (setmaxnreg); each role's
  * code sits after its own setmaxnreg so the compiler budgets it alone.
- * Every wait is bounded (ST_TIMEOUT).
+ * Every wait is bounded (ST_TIMEOUT): about a second in the instantiations a
+ * step uses.  TW selects the fault-injection instantiation that tests of the
+ * timeout path run (tria_ctx_set_wait_limit): its waits poll up to the
+ * context's shortened bound and give up in every lane of a warp at once; it
+ * is a separate kernel so that the runtime bound costs the step nothing.
  */
-template <int KT, int G, int SC_T, bool DT>
+template <int KT, int G, int SC_T, bool DT, bool TW = false>
 __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a, const WsPlan plan) {
     constexpr int FC = 64, NQ = FC / 2, QPL = 4;        /* pairs per lane */
     constexpr int WS_CPL = SC_T / 4;                     /* cells per lane: a warp's tile cells in one pass */
@@ -587,7 +604,15 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         for (int k = 0; k < n_mine; k++) {
             const int c0 = t * SC_T;
             const int cells = max(0, min(SC_T, a.layer_rows[l] - c0));
-            if (!warp_wait(&full[st], phase, &s_wait_limit, &s_abort, a.status)) break;
+            if constexpr (TW) {
+                if (!warp_wait(&full[st], phase, &s_wait_limit, &s_abort, a.status)) break;
+            } else {
+                if (!mbar_wait(&full[st], phase)) {
+                    if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
+                    s_abort = 1;
+                }
+                if (s_abort) break;
+            }
             const uint8_t *sb = stages + st * stage_bytes;
             const uint8_t *tab = sb + plan.k_bytes();
             const int32_t *slot = reinterpret_cast<const int32_t *>(tab + plan.tab_bytes(FC));
@@ -680,11 +705,19 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);           /* the stage is no longer read */
             /* partial sums -> buffer pk once the reducers are done with its previous item */
-            /* (a lighter uniform form than warp_wait: the G accumulators are live here;
-             * another warp's abort is seen at the next stage wait) */
-            if (__any_sync(0xffffffffu, !mbar_wait(&pfree[pk], pph ^ 1u, s_wait_limit))) {
-                if (lane == 0) { atomicOr(a.status, ST_TIMEOUT); s_abort = 1; }
-                break;
+            if constexpr (TW) {
+                /* (a lighter uniform form than warp_wait: the G accumulators are live
+                 * here; another warp's abort is seen at the next stage wait) */
+                if (!warp_wait_light(&pfree[pk], pph ^ 1u, &s_wait_limit)) {
+                    if (lane == 0) { atomicOr(a.status, ST_TIMEOUT); s_abort = 1; }
+                    break;
+                }
+            } else {
+                if (!mbar_wait(&pfree[pk], pph ^ 1u)) {
+                    if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
+                    s_abort = 1;
+                }
+                if (s_abort) break;
             }
             if (cb < cend) {
                 float *pb = part + pk * plan.part_floats();
@@ -742,12 +775,21 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         for (; pos_issued < min(WS_POS_RING - 1, n_mine); pos_issued++) fetch_pos(pos_issued);
         int k = 0;
         for (; k < n_mine; k++) {
-            if (__any_sync(0xffffffffu, s_abort != 0)) break;
+            if (TW ? __any_sync(0xffffffffu, s_abort != 0) : s_abort != 0) break;
             const int st = k % S;
             if (pos_issued < n_mine) fetch_pos(pos_issued++);   /* ring slot of item k-1: done with */
-            if (!warp_wait(&posbar[k % WS_POS_RING], (uint32_t)((k / WS_POS_RING) & 1), &s_wait_limit, &s_abort, a.status) ||
-                !warp_wait(&empty[st], (uint32_t)(((k / S) & 1) ^ 1), &s_wait_limit, &s_abort, a.status))
-                break;
+            if constexpr (TW) {
+                if (!warp_wait(&posbar[k % WS_POS_RING], (uint32_t)((k / WS_POS_RING) & 1), &s_wait_limit, &s_abort, a.status) ||
+                    !warp_wait(&empty[st], (uint32_t)(((k / S) & 1) ^ 1), &s_wait_limit, &s_abort, a.status))
+                    break;
+            } else {
+                if (!mbar_wait(&posbar[k % WS_POS_RING], (uint32_t)((k / WS_POS_RING) & 1)) ||
+                    !mbar_wait(&empty[st], (uint32_t)(((k / S) & 1) ^ 1))) {
+                    if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
+                    s_abort = 1;
+                    break;
+                }
+            }
             /* the consumers' reads of this stage happen before these async writes */
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             int l, c0;
@@ -823,7 +865,15 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
         int pk = 0;
         uint32_t pph = 0;
         for (int k = 0; k < n_mine; k++) {
-            if (!warp_wait(&pfull[pk], pph, &s_wait_limit, &s_abort, a.status)) break;
+            if constexpr (TW) {
+                if (!warp_wait(&pfull[pk], pph, &s_wait_limit, &s_abort, a.status)) break;
+            } else {
+                if (!mbar_wait(&pfull[pk], pph)) {
+                    if (lane == 0) atomicOr(a.status, ST_TIMEOUT);
+                    s_abort = 1;
+                }
+                if (s_abort) break;
+            }
             const int c0 = t * SC_T;
             const int cells = max(0, min(SC_T, a.layer_rows[l] - c0));
             const float *pb = part + pk * plan.part_floats();
