@@ -987,6 +987,16 @@ extern "C" TRIA_API int tria_znorm_stats(const float *x, int64_t stride, const i
 /* Page-locked (or managed / device) memory that kernels may read and write
  * through its own address.  Unregistered pageable memory is refused: a kernel
  * touching it would fault. */
+/* 1: device memory, 2: page-locked or managed host memory, 0: neither
+ * (pageable, unknown, or no device). */
+extern "C" int tria_memory_kind(const void *p) {
+    cudaPointerAttributes at;
+    if (!p || cudaPointerGetAttributes(&at, p) != cudaSuccess) { cudaGetLastError(); return 0; }
+    if (at.type == cudaMemoryTypeDevice) return 1;
+    if (at.type == cudaMemoryTypeHost || at.type == cudaMemoryTypeManaged) return 2;
+    return 0;
+}
+
 static bool device_accessible(const void *p) {
     cudaPointerAttributes at;
     if (cudaPointerGetAttributes(&at, p) != cudaSuccess) { cudaGetLastError(); return false; }

@@ -22,6 +22,10 @@ void tria_set_error(const char *fmt, ...);
 /* Destroy the device contexts tria_score_kv_head cached for `stats`. */
 void tria_release_stats_contexts(const struct tria_stats *stats);
 
+/* Where `p` lives: 1 device memory, 2 page-locked or managed host memory,
+ * 0 anything else (pageable memory, an unknown pointer, no device). */
+int tria_memory_kind(const void *p);
+
 #ifdef __cplusplus
 }
 #endif

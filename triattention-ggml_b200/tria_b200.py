@@ -25,6 +25,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libtriattention_b200.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "triattention.h")
+HEADERS = [HEADER, os.path.join(os.path.dirname(HERE), "include", "triattention_ggml.h")]
 
 TYPE_F16 = 1
 TYPE_Q8_0 = 8
@@ -68,6 +69,53 @@ class KvView(C.Structure):
 
 
 VIEW_POST_ROPE = 1      # TRIA_VIEW_POST_ROPE
+
+
+class GgmlTensor(C.Structure):
+    """struct tria_ggml_tensor: the ggml_tensor fields the bridge reads."""
+    _fields_ = [("type", C.c_int32), ("reserved", C.c_int32), ("ne", C.c_int64 * 4),
+                ("nb", C.c_size_t * 4), ("data", C.c_void_p)]
+
+
+class GgmlCache(C.Structure):
+    """struct tria_ggml_cache."""
+    _fields_ = [("k", C.POINTER(C.POINTER(GgmlTensor))), ("v", C.POINTER(C.POINTER(GgmlTensor))),
+                ("n_layer", C.c_int32), ("layer0", C.c_int32), ("n_head_kv", C.c_int32),
+                ("head_dim", C.c_int32), ("pos", C.c_void_p), ("pos_shared", C.c_int32),
+                ("flags", C.c_int32)]
+
+
+def ggml_tensor(type_id, ne0, ne1, nb1, data, elem=None):
+    """A 2-D ggml tensor descriptor [ne0, ne1] with rows nb1 bytes apart."""
+    t = GgmlTensor()
+    t.type = int(type_id)
+    t.ne[:] = [int(ne0), int(ne1), 1, 1]
+    e = elem if elem is not None else (2 if type_id == TYPE_F16 else 34)
+    t.nb[:] = [e, int(nb1), int(nb1) * int(ne1), int(nb1) * int(ne1)]
+    t.data = _ptr(data)
+    return t
+
+
+def ggml_cache(k_tensors, v_tensors, n_head_kv, head_dim, pos, layer0=0, pos_shared=False, flags=0):
+    """A GgmlCache over lists of GgmlTensor; keeps its arrays alive."""
+    nl = len(k_tensors)
+    karr = (C.POINTER(GgmlTensor) * nl)(*[C.pointer(t) for t in k_tensors])
+    varr = (C.POINTER(GgmlTensor) * nl)(*[C.pointer(t) for t in v_tensors]) if v_tensors is not None else None
+    c = GgmlCache(C.cast(karr, C.POINTER(C.POINTER(GgmlTensor))),
+                  C.cast(varr, C.POINTER(C.POINTER(GgmlTensor))) if varr is not None else None,
+                  nl, int(layer0), int(n_head_kv), int(head_dim), _ptr(pos), 1 if pos_shared else 0, int(flags))
+    c._keep = (karr, varr, k_tensors, v_tensors, pos)
+    return c
+
+
+def ggml_view(cache):
+    """tria_ggml_view: (status, KvView) without raising."""
+    nl = cache.n_layer
+    kp, vp = (C.c_void_p * nl)(), (C.c_void_p * nl)()
+    v = KvView()
+    r = lib().tria_ggml_view(C.byref(cache), C.byref(v), kp, vp)
+    v._keep = (kp, vp, cache)
+    return r, v
 
 
 class EvictParams(C.Structure):
@@ -143,6 +191,9 @@ def lib() -> C.CDLL:
         L.tria_ctx_launches.restype = C.c_int64
         L.tria_ctx_launches.argtypes = [C.c_void_p]
         L.tria_ctx_check.argtypes = [C.c_void_p, C.c_void_p]
+        L.tria_ggml_view.argtypes = [C.POINTER(GgmlCache), C.POINTER(KvView), C.c_void_p, C.c_void_p]
+        L.tria_ggml_evict.argtypes = [C.c_void_p, C.POINTER(GgmlCache), C.POINTER(GgmlCache), C.c_void_p,
+                                      C.POINTER(EvictParams), C.c_void_p]
         L.tria_ctx_set_wait_limit.argtypes = [C.c_void_p, C.c_int64]
         L.tria_select_noalloc.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int32,
                                           C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
@@ -166,10 +217,13 @@ def lib() -> C.CDLL:
     return _lib
 
 
-def exported_symbols_in_header(path: str = HEADER):
-    """Names of every function the header declares with TRIA_API."""
-    txt = open(path).read()
-    return sorted(set(re.findall(r"TRIA_API\s+[^;(]*?\b(tria_\w+)\s*\(", txt)))
+def exported_symbols_in_header(paths=None):
+    """Names of every function the public headers declare with TRIA_API."""
+    names = set()
+    for path in paths or HEADERS:
+        txt = open(path).read()
+        names |= set(re.findall(r"TRIA_API\s+[^;(]*?\b(tria_\w+)\s*\(", txt))
+    return sorted(names)
 
 
 def last_error() -> str:
@@ -339,6 +393,11 @@ class Context:
         a, p = self._rows(n_rows)
         check(lib().tria_evict(self.h, C.byref(src), C.byref(dst), p, C.byref(params),
                                _ptr(n_kept_out), _stream(stream)))
+
+    def ggml_evict(self, src, dst, n_rows, params, stream=None):
+        """tria_ggml_evict: one step on ggml-described caches (GgmlCache)."""
+        a, p = self._rows(n_rows)
+        check(lib().tria_ggml_evict(self.h, C.byref(src), C.byref(dst), p, C.byref(params), _stream(stream)))
 
     def evict_host(self, src, dst, n_rows, params, stream=None):
         """tria_evict_host: src/dst views over page-locked host buffers."""
