@@ -84,10 +84,20 @@ def step_bytes(c, units, keep):
 
 
 def score_kernel_bytes(c, units, layers):
-    """Algorithmic DRAM bytes of one scoring launch over `units` (layer, kv-head)
-    units of n rows: every K row once, the shared position row once per layer,
-    the delta table rows once (n rows of fc*8 bytes), and the G raw scores of
-    every row written."""
+    """Algorithmic bytes of one scoring launch over `units` (layer, kv-head)
+    units of n rows, the scoring share of the step's bytes: every K row read
+    once (n*Rb per unit) and its position (4*n per unit).  The raw scores it
+    writes and the delta-table rows it reads are intermediates of the step."""
+    rb = workloads.row_bytes(c["type"], c["hd"])
+    n = c["n"]
+    return units * (n * rb + 4 * n)
+
+
+def score_kernel_traffic_bytes(c, units, layers):
+    """What the scoring launch must move at least, intermediates included:
+    every K row once, the shared position row once per layer, the delta table
+    rows once (n rows of fc*8 bytes), and the G raw scores of every row
+    written (the figure ncu's DRAM traffic is compared with)."""
     rb = workloads.row_bytes(c["type"], c["hd"])
     n, G, fc = c["n"], c["H"] // c["KV"], c["hd"] // 2
     return units * n * rb + layers * n * 4 + n * fc * 8 + units * G * n * 4
@@ -460,6 +470,7 @@ def run_ours(args):
                      "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
                      "traffic": traffic, "peak_source": f"{peak_src} hbm_gbs",
                      "algorithmic_bytes_per_launch": sb, "launch_ms": score_ms,
+                     "bytes_with_intermediates_per_launch": score_kernel_traffic_bytes(c, units, L),
                      "fp32_flops_per_launch": flops,
                      "fp32_tflops": flops / (score_ms / 1e3) / 1e12 if score_ms else None},
         "step_roofline": {"bytes_per_step": step_b, "achieved": step_b / (ms / 1e3) / 1e9,
@@ -613,10 +624,8 @@ def run_ramp(args):
     keeps = [int(workloads.layer_keep(int(r[0]), budget, p.ramp_pct)) for r, p in zip(rows, params)]
     step_b = [int(r.sum()) * rb + 4 * units * k * rb + 4 * int(r.sum()) + 8 * units * k for r, k in zip(rows, keeps)]
     step_ms = [sum(v for kk, v in d.items() if kk != "table") for d in per_step]
-    # K rows, positions (one shared row per layer on the first step, per head after),
-    # table rows, G raw scores per row
-    score_b = [int(r.sum()) * rb + (L * int(r[0]) if t == 0 else int(r.sum())) * 4 + int(r.max()) * (hd // 2) * 8
-               + (c["H"] // KV) * int(r.sum()) * 4 for t, r in enumerate(rows)]
+    # the scoring share of each step's algorithmic bytes: K rows and their positions
+    score_b = [int(r.sum()) * (rb + 4) for r in rows]
     score_ms = [d["score"] for d in per_step]
     peak, peak_src = measured_peak()
     ach = sum(score_b) / (sum(score_ms) / 1e3) / 1e9
