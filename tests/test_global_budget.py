@@ -70,6 +70,20 @@ def test_boundary_bin():
     assert gb.boundary_bin(h, 10) == (10, 5)
 
 
+def test_boundary_bins_match_boundary_bin():
+    """The batched (torch) search gives boundary_bin's answer on every row."""
+    import torch
+    rng = np.random.default_rng(0)
+    h = np.zeros((5, gb.NBINS), np.int64)
+    for s in range(5):
+        idx = rng.integers(0, gb.NBINS, 40)
+        np.add.at(h[s], idx, rng.integers(1, 50, 40))
+    h[4, -1] = 7                                  # a key in the top bin
+    needs = [1, int(h[1].sum()), int(h[2].sum()) // 2, 17, 3]
+    got = gb.boundary_bins(torch.from_numpy(h), needs)
+    assert got == [gb.boundary_bin(h[s], needs[s]) for s in range(5)]
+
+
 def test_score_keys_match_the_library():
     import tria_b200
     x = np.array([0.0, -0.0, 1.5, -1.5, np.inf, -np.inf, np.nan, 1e-40, -1e-40], np.float32)

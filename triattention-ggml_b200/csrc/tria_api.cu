@@ -1195,9 +1195,22 @@ extern "C" TRIA_API int tria_key_histogram(const float *scores, int64_t score_st
         a->hist = hist;
         int mx = 0;
         for (int u = 0; u < nu; u++) { a->n_rows[u] = n_rows[u0 + u]; mx = std::max(mx, a->n_rows[u]); }
-        if (mx > 0) k_key_hist<<<dim3((unsigned)std::min((mx + 255) / 256, 64), (unsigned)nu), 256, 0,
-                                 (cudaStream_t)stream>>>(*a);
+        cudaError_t e = cudaSuccess;
+        if (mx > 0 && level == 0) {             /* per-block histograms in shared memory */
+            static bool attr_set = false;
+            if (!attr_set) {
+                e = cudaFuncSetAttribute(k_key_hist0_smem, cudaFuncAttributeMaxDynamicSharedMemorySize, KEY_HIST_SMEM);
+                attr_set = e == cudaSuccess;
+            }
+            if (e == cudaSuccess)
+                k_key_hist0_smem<<<dim3((unsigned)nu, (unsigned)((mx + KEY_HIST_ROWS - 1) / KEY_HIST_ROWS)),
+                                   SELECT_THREADS, KEY_HIST_SMEM, (cudaStream_t)stream>>>(*a);
+        } else if (mx > 0) {                    /* level 1: the few keys of one bin */
+            k_key_hist<<<dim3((unsigned)std::min((mx + 255) / 256, 64), (unsigned)nu), 256, 0,
+                         (cudaStream_t)stream>>>(*a);
+        }
         delete a;
+        if (e != cudaSuccess) FAIL(TRIA_ERR_CUDA, "tria_key_histogram: %s", cudaGetErrorString(e));
         CUDA_TRY(cudaGetLastError());
         return TRIA_OK;
     });

@@ -1830,14 +1830,51 @@ struct KeyArgs {
     int32_t n_rows[TRIA_MAX_UNITS];
 };
 
+/* The z-score keys of a unit crowd into a few hundred of the 65536 bins, so
+ * the lanes of a warp that fall into one bin add their count with a single
+ * atomic (__match_any_sync groups them; the group's lowest lane adds). */
 __global__ void __launch_bounds__(256) k_key_hist(const KeyArgs a) {
-    const int u = blockIdx.y;
+    const int u = blockIdx.y, lane = threadIdx.x & 31;
     const int n = a.n_rows[u];
     const float *sc = a.scores + (int64_t)u * a.score_stride;
-    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n; r += gridDim.x * blockDim.x) {
-        const uint32_t k = score_key(sc[r]);
-        if (a.level == 0) atomicAdd(&a.hist[k >> 16], 1u);
-        else if ((k >> 16) == a.key) atomicAdd(&a.hist[k & 0xffffu], 1u);
+    const int stride = gridDim.x * blockDim.x;
+    for (int r0 = blockIdx.x * blockDim.x + (threadIdx.x & ~31); r0 < n; r0 += stride) {   /* warp-uniform */
+        const int r = r0 + lane;
+        const uint32_t k = r < n ? score_key(sc[r]) : 0u;
+        const bool in = r < n && (a.level == 0 || (k >> 16) == a.key);
+        const uint32_t bin = in ? (a.level == 0 ? k >> 16 : k & 0xffffu) : 0xffffffffu;
+        const unsigned grp = __match_any_sync(0xffffffffu, bin);
+        if (in && lane == __ffs(grp) - 1) atomicAdd(&a.hist[bin], (uint32_t)__popc(grp));
+    }
+}
+
+/* Level 0 (the keys' high halves) with a private histogram per block: the
+ * 65536 bins as 16-bit counters, two to a word, in 128 KB of shared memory;
+ * block (u, part) counts rows [part * KEY_HIST_ROWS, ...) of unit u (at most
+ * KEY_HIST_ROWS < 2^16, so no counter overflows) and then adds its non-zero
+ * bins to the global histogram.  The z-scores of a sequence crowd into a few
+ * hundred bins, where global atomics from every block would serialise. */
+constexpr int KEY_HIST_ROWS = 32768;
+constexpr int KEY_HIST_SMEM = (1 << 16) * 2;
+__global__ void __launch_bounds__(SELECT_THREADS, 1) k_key_hist0_smem(const KeyArgs a) {
+    extern __shared__ __align__(16) uint32_t s_h[];             /* [32768] words: bins 2w (low half), 2w+1 (high) */
+    const int u = blockIdx.x;
+    const int n = a.n_rows[u];
+    const int r0 = blockIdx.y * KEY_HIST_ROWS, r1 = min(n, r0 + KEY_HIST_ROWS);
+    if (r0 >= r1) return;                                        /* uniform: nothing of this unit here */
+    for (int i = threadIdx.x; i < (1 << 15) / 4; i += blockDim.x)
+        reinterpret_cast<uint4 *>(s_h)[i] = make_uint4(0u, 0u, 0u, 0u);
+    __syncthreads();
+    const float *sc = a.scores + (int64_t)u * a.score_stride;
+    for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+        const uint32_t bin = score_key(sc[r]) >> 16;
+        atomicAdd(&s_h[bin >> 1], 1u << (16 * (bin & 1)));
+    }
+    __syncthreads();
+    for (int w = threadIdx.x; w < (1 << 15); w += blockDim.x) {
+        const uint32_t v = s_h[w];
+        if (v & 0xffffu) atomicAdd(&a.hist[2 * w], v & 0xffffu);
+        if (v >> 16) atomicAdd(&a.hist[2 * w + 1], v >> 16);
     }
 }
 

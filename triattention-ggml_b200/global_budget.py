@@ -42,13 +42,54 @@ def boundary_bin(hist, need):
     return b, int(need - above)
 
 
+def boundary_bins(hists, needs):
+    """boundary_bin for every row of hists [n_seq, NBINS] at once (need >= 1),
+    on the tensor's own device: only the (bin, need) pairs come back."""
+    import torch
+    h = hists.to(torch.int64)
+    from_top = torch.cumsum(h.flip(1), dim=1)
+    nd = torch.as_tensor(needs, dtype=torch.int64, device=h.device).reshape(-1, 1)
+    i = torch.searchsorted(from_top, nd).clamp_(max=NBINS - 1)
+    b = NBINS - 1 - i
+    rest = nd - (from_top.gather(1, i) - h.gather(1, b))
+    res = torch.cat([b, rest], 1).cpu().numpy()
+    return [(int(x), int(y)) for x, y in res]
+
+
 class DeviceBackend:
     """The GPU path: z-max scores on the device ([units][stride] fp32) of the
-    units this rank owns for one sequence, processed through the C ABI."""
+    units this rank owns for one sequence, processed through the C ABI.
+    histograms() fills one preallocated [n_seq, NBINS] buffer for all
+    sequences of a level, so a level costs one copy and one gather."""
 
     def __init__(self, device, stream=None):
         self.device = device
         self.stream = stream
+        self._hbuf = None
+
+    def histograms(self, seqs, level, prefixes):
+        import torch
+        import tria_b200
+        n = len(seqs)
+        if self._hbuf is None or self._hbuf.shape[0] < n:
+            self._hbuf = torch.zeros((n, NBINS), dtype=torch.int32, device=self.device)
+        h = self._hbuf[:n]
+        h.zero_()
+        for s, (sq, p) in enumerate(zip(seqs, prefixes)):
+            tria_b200.key_histogram(sq["scores"], sq["stride"], sq["n_rows"], level, p, h[s], self.stream)
+        return h
+
+    def counts(self, seqs, keys):
+        """count() for every sequence into one buffer; returns [n_seq] int64 totals."""
+        import torch
+        import tria_b200
+        width = max(len(sq["n_rows"]) for sq in seqs)
+        buf = torch.zeros((len(seqs), width), dtype=torch.int32, device=self.device)
+        for s, (sq, key) in enumerate(zip(seqs, keys)):
+            c = buf[s, :len(sq["n_rows"])]
+            tria_b200.key_count(sq["scores"], sq["stride"], sq["n_rows"], key, c, self.stream)
+            sq["_counts"] = c
+        return buf.to(torch.int64).sum(1)
 
     def histogram(self, seq, level, prefix):
         import torch
@@ -83,34 +124,34 @@ def global_select(seqs, k_total, gather, backend, rank):
     """
     import torch
     n_seq = len(seqs)
-    # 1. high halves
-    h0 = torch.stack([backend.histogram(sq, 0, 0) for sq in seqs])
-    g0 = gather(h0).sum(0).cpu().numpy()
-    bins, needs = [], []
-    for s in range(n_seq):
-        total = int(g0[s].sum())
-        k = min(int(k_total[s]), total)
-        if k <= 0:
-            bins.append(None)
-            needs.append(0)
-            continue
-        b, need = boundary_bin(g0[s], k)
-        bins.append(b)
-        needs.append(need)
+
+    def level_hists(level, prefixes):
+        if hasattr(backend, "histograms"):
+            return backend.histograms(seqs, level, prefixes)
+        return torch.stack([backend.histogram(sq, level, p) for sq, p in zip(seqs, prefixes)])
+
+    # 1. high halves (the bin search runs where the summed histograms are;
+    #    the totals ride along in the same copy)
+    g0 = gather(level_hists(0, [0] * n_seq)).to(torch.int64).sum(0)
+    totals = g0.sum(1).cpu().numpy()
+    ks = [min(int(k_total[s]), int(totals[s])) for s in range(n_seq)]
+    live = [s for s in range(n_seq) if ks[s] > 0]
+    bins, needs = [None] * n_seq, [0] * n_seq
+    if live:
+        for s, (b, need) in zip(live, boundary_bins(g0[live], [ks[s] for s in live])):
+            bins[s], needs[s] = b, need
     # 2. low halves inside the boundary bins
-    h1 = torch.stack([backend.histogram(sq, 1, b if b is not None else 0) for sq, b in zip(seqs, bins)])
-    g1 = gather(h1).sum(0).cpu().numpy()
-    keys, needs2 = [], []
-    for s in range(n_seq):
-        if bins[s] is None:
-            keys.append(0xFFFFFFFF)              # nothing above it, no rows equal to it allowed
-            needs2.append(0)
-            continue
-        t, need2 = boundary_bin(g1[s], needs[s])
-        keys.append((bins[s] << 16) | t)
-        needs2.append(need2)
+    g1 = gather(level_hists(1, [b if b is not None else 0 for b in bins])).to(torch.int64).sum(0)
+    keys, needs2 = [0xFFFFFFFF] * n_seq, [0] * n_seq   # dead sequences: nothing above the key, no ties allowed
+    if live:
+        for s, (t, need2) in zip(live, boundary_bins(g1[live], [needs[s] for s in live])):
+            keys[s] = (bins[s] << 16) | t
+            needs2[s] = need2
     # 3. rows equal to the threshold, in rank (layer) order
-    ties = torch.stack([backend.count(sq, key).sum() for sq, key in zip(seqs, keys)])
+    if hasattr(backend, "counts"):
+        ties = backend.counts(seqs, keys)
+    else:
+        ties = torch.stack([backend.count(sq, key).sum() for sq, key in zip(seqs, keys)])
     gt = gather(ties).cpu().numpy()              # [world, n_seq]
     out = []
     for s in range(n_seq):
