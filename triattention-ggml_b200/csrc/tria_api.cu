@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <new>
 #include <vector>
@@ -23,6 +24,25 @@
 #include "tria_kernels.cuh"
 
 using namespace tria;
+
+/* Raises a kernel's dynamic shared-memory limit on the current device to at
+ * least `bytes`.  The attribute belongs to each device's copy of the kernel
+ * (a process may drive several GPUs, as llama.cpp does when it splits layers),
+ * so it is tracked per (kernel, device) and set only when a launch needs more
+ * than before. */
+static cudaError_t raise_smem_limit(const void *fn, int bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void *, int>, int> set_to;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    int &have = set_to[{fn, dev}];
+    if (bytes <= have) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) have = bytes;
+    return e;
+}
 
 /* ------------------------------------------------------------------ */
 /* Errors                                                               */
@@ -448,13 +468,8 @@ static cudaError_t launch_znorm_chains(const ZArgs &z, int chains, int sm_count,
         k_znorm_seg<<<chains, ZS_WARPS * 32, 0, st>>>(z);
         return cudaGetLastError();
     }
-    static bool attr_set = false;          /* the opt-in maximum, once per process (per device is not needed: same limit) */
-    if (!attr_set) {
-        const cudaError_t e = cudaFuncSetAttribute(k_znorm_pre, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   zp_smem_bytes(ZP_MAX_SEG));
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    const cudaError_t e = raise_smem_limit((const void *)k_znorm_pre, (int)zp_smem_bytes(ZP_MAX_SEG));
+    if (e != cudaSuccess) return e;
     k_znorm_pre<<<chains, ZP_WARPS * 32, zp_smem_bytes(nseg), st>>>(z);
     return cudaGetLastError();
 }
@@ -522,7 +537,7 @@ static int launch_ws_inst(const TmaScoreArgs &a, const WsPlan &plan, int grid, c
         FAIL(TRIA_ERR_UNSUPPORTED, "k_score_ws: compiled with %d registers per thread, its register split needs %d",
              regs, WS_LAUNCH_REGS);
     const int smem = plan.total(64);
-    CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CUDA_TRY(raise_smem_limit((const void *)fn, smem));
     fn<<<grid, WS_THREADS, smem, st>>>(a, plan);
     CUDA_TRY(cudaGetLastError());
     return TRIA_OK;
@@ -691,14 +706,8 @@ static int launch_select(tria_ctx *c, const tria_kv_view *v, const int32_t *n_ro
         for (int u = 0; u < units; u++) n_max = std::max(n_max, a->n_rows[u]);
         cudaError_t e = cudaSuccess;
         if (n_max <= SELECT_SMEM_KEYS) {       /* the unit's keys in shared memory */
-            static bool attr_set = false;
-            if (!attr_set) {
-                const size_t mx = (size_t)SELECT_SMEM_KEYS * 4;
-                e = cudaFuncSetAttribute(k_select<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mx);
-                if (e == cudaSuccess)
-                    e = cudaFuncSetAttribute(k_select<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mx);
-                attr_set = e == cudaSuccess;
-            }
+            e = raise_smem_limit(fused ? (const void *)k_select<true, true> : (const void *)k_select<false, true>,
+                                 SELECT_SMEM_KEYS * 4);
             const size_t smem = (size_t)std::max(n_max, 1) * 4;
             if (e == cudaSuccess) {
                 if (fused) k_select<true, true><<<units, SELECT_BLOCK_SM, smem, st>>>(*a);
@@ -1197,11 +1206,7 @@ extern "C" TRIA_API int tria_key_histogram(const float *scores, int64_t score_st
         for (int u = 0; u < nu; u++) { a->n_rows[u] = n_rows[u0 + u]; mx = std::max(mx, a->n_rows[u]); }
         cudaError_t e = cudaSuccess;
         if (mx > 0 && level == 0) {             /* per-block histograms in shared memory */
-            static bool attr_set = false;
-            if (!attr_set) {
-                e = cudaFuncSetAttribute(k_key_hist0_smem, cudaFuncAttributeMaxDynamicSharedMemorySize, KEY_HIST_SMEM);
-                attr_set = e == cudaSuccess;
-            }
+            e = raise_smem_limit((const void *)k_key_hist0_smem, KEY_HIST_SMEM);
             if (e == cudaSuccess)
                 k_key_hist0_smem<<<dim3((unsigned)nu, (unsigned)((mx + KEY_HIST_ROWS - 1) / KEY_HIST_ROWS)),
                                    SELECT_THREADS, KEY_HIST_SMEM, (cudaStream_t)stream>>>(*a);
