@@ -273,6 +273,13 @@ TRIA_API int tria_ctx_check(tria_ctx *ctx, void *stream);
  * tria_get_n_kv / tria_ctx_check and leaves the context usable. */
 TRIA_API int tria_ctx_set_wait_limit(tria_ctx *ctx, int64_t cycles);
 
+/* Tuning: the most CTAs that selection may give one (layer, kv-head) unit
+ * (up to 8).  0, the default, lets the library split a unit over a
+ * thread-block cluster of 2 CTAs when a launch has fewer units than SMs; 1
+ * keeps one block per unit.  Results are the same either way.  New; no
+ * reference counterpart. */
+TRIA_API int tria_ctx_set_select_split(tria_ctx *ctx, int32_t max_ctas);
+
 /* Device-pointer form of tria_score_kv_head for one (layer, kv-head):
  * k_re/k_im [n][fc] fp32, key_pos [n] int32, out [n] fp32, all device. */
 TRIA_API int tria_score_kv_head_dev(tria_ctx *ctx, const float *k_re, const float *k_im,

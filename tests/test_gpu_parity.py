@@ -186,17 +186,22 @@ def test_tria_score_cache_vs_oracle(torch_dev, oracle, tmp_path_factory, type_id
         oracle.free(ost)
 
 
-@pytest.mark.parametrize("seed,n_cells", [(0, 5000), (1, 5000), (2, 5000), (3, 5000), (1, 40000), (2, 70000)])
-def test_tria_select_exact_on_oracle_scores(torch_dev, oracle, synth_stats_path, seed, n_cells):
+@pytest.mark.parametrize("split", [0, 1, 3])
+@pytest.mark.parametrize("seed,n_cells", [(0, 5000), (1, 5000), (2, 5000), (3, 5000), (1, 40000), (2, 70000),
+                                          (3, 131000)])
+def test_tria_select_exact_on_oracle_scores(torch_dev, oracle, synth_stats_path, seed, n_cells, split):
     """Selection alone: the GPU radix select on the oracle's own scores must
     return the oracle's index sets exactly (ties, NaN, signed zeros, window,
-    sink), up to units of 70000 rows (several 32-row chunks per warp)."""
+    sink), up to units of 131000 rows (several 32-row chunks per warp).  With
+    8 units the default (split 0) gives each unit a cluster of 8 CTAs, split 3
+    a cluster of 3 (uneven shares), split 1 one block per unit."""
     import torch
     rng = np.random.default_rng(seed)
     L, KV, hd = 2, 4, 128
     st = tria_b200.load(synth_stats_path)
     try:
         ctx = tria_b200.Context(st, 0)
+        ctx.set_select_split(split)
         scores = rng.standard_normal((L * KV, n_cells)).astype(np.float32)
         if seed % 2:
             scores = (np.round(scores * 4) / 4).astype(np.float32)     # heavy ties

@@ -137,6 +137,7 @@ struct tria_ctx {
     /* status / counts read-back */
     int32_t *d_status = nullptr;         /* ST_* bits the kernels set; cleared when read back */
     long long wait_limit = WAIT_LIMIT_DEFAULT;   /* bound of the scoring kernel's pipeline waits */
+    int select_split = 0;                        /* CTAs per unit in selection: 0 automatic, 1 one block */
     int32_t *h_pinned = nullptr;         /* [0] = status, [1..] counts */
     int32_t pinned_cap = 0;
     int32_t last_units = 0;
@@ -453,12 +454,13 @@ static void fill_score_args(const tria_ctx *c, const tria_kv_view *v, const int3
 
 /* The z-norm statistics of z.units * z.G chains.  Both kernels are exact;
  * they differ in latency and throughput (measured on B200, 32768-element
- * chains): k_znorm_pre (records of a whole pass at once, 8 warps a chain)
- * finishes a chain sooner when few chains share the GPU (128 chains: 66 us
- * against 76 us), k_znorm_seg (window by window, 4 warps a chain, 8 chains an
- * SM) keeps more chains going at once and wins from a few chains per SM on
- * (1152 chains: 136 us against 160-190 us).  k_znorm_pre also needs the
- * longest chain to fit its shared-memory plan. */
+ * chains): k_znorm_pre (records of a whole pass at once, 16 warps a chain,
+ * two chains an SM) finishes a chain sooner when few chains share the GPU
+ * (148 chains: 45 us, 296 chains: 55 us, against 76 us for k_znorm_seg at
+ * 128), k_znorm_seg (window by window, 4 warps a chain, 8 chains an SM) keeps
+ * more chains going at once and wins from a few chains per SM on (1152
+ * chains: 136 us against 160-190 us).  k_znorm_pre also needs the longest
+ * chain to fit its shared-memory plan. */
 static cudaError_t launch_znorm_chains(const ZArgs &z, int chains, int sm_count, cudaStream_t st) {
     if (chains <= 0) return cudaSuccess;
     int n_max = 0;
@@ -672,6 +674,57 @@ static void keep_requests(const tria_ctx *c, const tria_kv_view *v, const int32_
     }
 }
 
+/* Clusters of `cl` k_select_cl CTAs that can run at once on this device (one
+ * CTA per SM at the largest key share), cached per (device, kernel, cl). */
+static int max_active_clusters(bool fused, int cl) {
+    static std::mutex mu;
+    static std::map<std::pair<int, int>, int> known;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    const int key = (fused ? 16 : 0) + cl;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = known.find({dev, key});
+    if (it != known.end()) return it->second;
+    auto fn = fused ? k_select_cl<true> : k_select_cl<false>;
+    const int smem = SELECT_SMEM_KEYS * 4;
+    int n = 0;
+    if (raise_smem_limit((const void *)fn, smem) == cudaSuccess) {
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = (unsigned)cl;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)cl);
+        cfg.blockDim = dim3(SELECT_BLOCK_SM);
+        cfg.dynamicSmemBytes = (size_t)smem;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, (const void *)fn, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();
+    known[{dev, key}] = n;
+    return n;
+}
+
+/* CTAs per unit for selection.  With fewer units than SMs (a rank's share of
+ * the layers) one block per unit leaves most SMs idle, so each unit gets a
+ * cluster of CTAs: up to the cap, the largest size for which every unit's
+ * cluster runs in one wave and a CTA's share of the keys fits in its shared
+ * memory.  1 means k_select. */
+static int select_split(const tria_ctx *c, int units, int n_max, bool fused) {
+    if (c->select_split == 1 || units <= 0) return 1;
+    /* automatic: two CTAs.  Measured on B200 (32768-row units, 40 units):
+     * 44 us with one block, 36 us with two, 40 us with three or four; more
+     * CTAs spend what they save on reading each other's histograms. */
+    const int cap = c->select_split > 1 ? std::min(c->select_split, 8) : 2;
+    for (int cl = std::min(cap, c->sm_count / units); cl >= 2; cl--) {
+        if (select_cl_chunk(n_max, cl) > SELECT_SMEM_KEYS) break;    /* fewer CTAs: larger shares */
+        if (units <= max_active_clusters(fused, cl)) return cl;
+    }
+    return 1;
+}
+
 static int launch_select(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, const std::vector<int32_t> &keep,
                          const tria_evict_params *p, bool fused, const float *scores, int32_t *kept_idx,
                          int64_t kept_stride, int32_t *n_kept, cudaStream_t st) {
@@ -705,15 +758,32 @@ static int launch_select(tria_ctx *c, const tria_kv_view *v, const int32_t *n_ro
         int n_max = 0;
         for (int u = 0; u < units; u++) n_max = std::max(n_max, a->n_rows[u]);
         cudaError_t e = cudaSuccess;
-        if (n_max <= SELECT_SMEM_KEYS) {       /* the unit's keys in shared memory */
-            e = raise_smem_limit(fused ? (const void *)k_select<true, true> : (const void *)k_select<false, true>,
-                                 SELECT_SMEM_KEYS * 4);
-            const size_t smem = (size_t)std::max(n_max, 1) * 4;
+        const int split = select_split(c, units, n_max, fused);
+        if (split > 1) {                       /* a cluster of `split` CTAs per unit, keys in shared memory */
+            auto fn = fused ? k_select_cl<true> : k_select_cl<false>;
+            const int smem = select_cl_chunk(n_max, split) * 4;
+            e = raise_smem_limit((const void *)fn, smem);
             if (e == cudaSuccess) {
-                if (fused) k_select<true, true><<<units, SELECT_BLOCK_SM, smem, st>>>(*a);
-                else k_select<false, true><<<units, SELECT_BLOCK_SM, smem, st>>>(*a);
+                cudaLaunchAttribute at[1];
+                at[0].id = cudaLaunchAttributeClusterDimension;
+                at[0].val.clusterDim.x = (unsigned)split;
+                at[0].val.clusterDim.y = 1;
+                at[0].val.clusterDim.z = 1;
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3((unsigned)(units * split));
+                cfg.blockDim = dim3(SELECT_BLOCK_SM);
+                cfg.dynamicSmemBytes = (size_t)smem;
+                cfg.stream = st;
+                cfg.attrs = at;
+                cfg.numAttrs = 1;
+                e = cudaLaunchKernelEx(&cfg, fn, *a);
             }
-        } else if (fused) {
+        } else if (n_max <= SELECT_SMEM_KEYS) {       /* one block per unit, keys in shared memory */
+            auto fn = fused ? k_select<true, true> : k_select<false, true>;
+            e = raise_smem_limit((const void *)fn, SELECT_SMEM_KEYS * 4);
+            const size_t smem = (size_t)std::max(n_max, 1) * 4;
+            if (e == cudaSuccess) fn<<<units, SELECT_BLOCK_SM, smem, st>>>(*a);
+        } else if (fused) {                    /* keys in global memory */
             k_select<true, false><<<units, SELECT_BLOCK, 0, st>>>(*a);
         } else {
             k_select<false, false><<<units, SELECT_BLOCK, 0, st>>>(*a);
@@ -1305,6 +1375,13 @@ extern "C" TRIA_API int tria_ctx_check(tria_ctx *c, void *stream) {
     CUDA_TRY(cudaMemsetAsync(c->d_status, 0, 4, st));
     CUDA_TRY(cudaStreamSynchronize(st));
     return status_of_bits(bits, "tria_ctx_check");
+}
+
+extern "C" TRIA_API int tria_ctx_set_select_split(tria_ctx *c, int32_t max_ctas) {
+    if (!c) FAIL(TRIA_ERR_INVALID, "tria_ctx_set_select_split: null ctx");
+    if (max_ctas < 0) FAIL(TRIA_ERR_INVALID, "tria_ctx_set_select_split: max_ctas %d < 0", max_ctas);
+    c->select_split = max_ctas;
+    return TRIA_OK;
 }
 
 extern "C" TRIA_API int tria_ctx_set_wait_limit(tria_ctx *c, int64_t cycles) {

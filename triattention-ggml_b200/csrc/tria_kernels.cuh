@@ -37,6 +37,7 @@
  */
 #pragma once
 
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -1299,7 +1300,7 @@ __global__ void __launch_bounds__(ZS_WARPS * 32, 8) k_znorm_seg(const ZArgs a) {
  * a global load.  Per chain this is three reads of the chain (sums, pass 1,
  * pass 2) and two walks; all of a pass's records are independent.
  */
-constexpr int ZP_WARPS = 8;
+constexpr int ZP_WARPS = 16;                  /* two CTAs per SM at 64 registers: 148-296 chains in one wave */
 constexpr int ZP_SLOTS = 12;                  /* staged segments per pass */
 constexpr int ZP_MAX_SEG = 6144;              /* segments (x ZS_SEG elements) the shared plan holds */
 
@@ -1459,7 +1460,7 @@ __device__ float zp_pass(const float *x, int n, int nseg, Val val, const ZpSmem 
 
 /* One CTA per chain: (mean, std) of triattention.c:227-238, chains of up to
  * ZP_MAX_SEG * ZS_SEG elements. */
-__global__ void __launch_bounds__(ZP_WARPS * 32) k_znorm_pre(const ZArgs a) {
+__global__ void __launch_bounds__(ZP_WARPS * 32, 2) k_znorm_pre(const ZArgs a) {
     extern __shared__ __align__(16) uint8_t zsm[];
     __shared__ int s_nst;
     __shared__ float s_state;
@@ -1602,20 +1603,22 @@ __device__ __forceinline__ int block_suffix_sum(int v, int *s_warp) {
     return incl;
 }
 
-/* Writes, in row order, the rows r < n whose key(r) > T, and the first
- * `allow` rows whose key(r) == T, to kept[]; returns how many.  Each warp
- * takes a contiguous range of rows, 32 at a time, so the counting is two
- * ballots per 32 rows, the only block-wide step is one exchange of the warps'
- * counts, and the indices go out as coalesced stores. */
+/* The contiguous rows [w * per_w, (w + 1) * per_w) of n that warp w takes in
+ * the ordered output (whole 32-row chunks). */
+__device__ __forceinline__ int ordered_rows_per_warp(int n) {
+    const int nw = blockDim.x >> 5;
+    return ((n + nw - 1) / nw + 31) & ~31;
+}
+
+/* Per warp of the block: how many of its rows have key(r) > T (s_gt[w]) and
+ * key(r) == T (s_eq[w]); two ballots per 32 rows, 4 chunks in flight. */
 template <class KeyOf>
-__device__ __forceinline__ int ordered_keep(int n, uint32_t T, int allow, int32_t *kept, KeyOf key) {
-    __shared__ int s_gt[32], s_eq[32];
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int per_w = ((n + nw - 1) / nw + 31) & ~31;
+__device__ __forceinline__ void ordered_counts(int n, uint32_t T, KeyOf key, int *s_gt, int *s_eq) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int per_w = ordered_rows_per_warp(n);
     const int r0 = min(n, w * per_w), r1 = min(n, r0 + per_w);
-    const unsigned lt = (1u << lane) - 1u;
     int gt = 0, eq = 0;
-    for (int b = r0; b < r1; b += 128) {                 /* 4 chunks of 32 rows in flight */
+    for (int b = r0; b < r1; b += 128) {
         uint32_t kk[4];
 #pragma unroll
         for (int q = 0; q < 4; q++) kk[q] = b + 32 * q + lane < r1 ? key(b + 32 * q + lane) : 0u;
@@ -1627,14 +1630,32 @@ __device__ __forceinline__ int ordered_keep(int n, uint32_t T, int allow, int32_
         }
     }
     if (lane == 0) { s_gt[w] = gt; s_eq[w] = eq; }
-    __syncthreads();
-    int gt_before = 0, eq_before = 0, gt_all = 0, eq_all = 0;
+}
+
+/* Writes, in row order, the rows r < n whose key(r) > T, and the first
+ * `allow` rows (over the whole unit) whose key(r) == T, to kept[] as row0 + r;
+ * returns how many the unit keeps.  s_gt / s_eq hold every warp's counts
+ * (ordered_counts); totals() turns the block's into the counts before it and
+ * over the unit (SoloTotals: the block owns the unit).  Each warp writes its
+ * own contiguous row range as coalesced stores. */
+template <class KeyOf, class Totals>
+__device__ __forceinline__ int ordered_write(int n, uint32_t T, int allow, int32_t *kept, KeyOf key, int row0,
+                                             const int *s_gt, const int *s_eq, Totals totals) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int per_w = ordered_rows_per_warp(n);
+    const int r0 = min(n, w * per_w), r1 = min(n, r0 + per_w);
+    const unsigned lt = (1u << lane) - 1u;
+    int gt_before = 0, eq_before = 0, gt_blk = 0, eq_blk = 0;
     for (int i = 0; i < nw; i++) {
         const int g = s_gt[i], e = s_eq[i];
         if (i < w) { gt_before += g; eq_before += e; }
-        gt_all += g;
-        eq_all += e;
+        gt_blk += g;
+        eq_blk += e;
     }
+    const int4 t = totals(gt_blk, eq_blk);               /* rows of the unit before this block's */
+    gt_before += t.x;
+    eq_before += t.y;
+    const int gt_all = t.z, eq_all = t.w;
     const int al = max(allow, 0);
     int out = gt_before + min(eq_before, al);
     int eqr = eq_before;
@@ -1649,7 +1670,7 @@ __device__ __forceinline__ int ordered_keep(int n, uint32_t T, int allow, int32_
             const unsigned em = __ballot_sync(0xffffffffu, e);
             const bool kp = r < r1 && (kk[q] > T || (e && eqr + __popc(em & lt) < al));
             const unsigned km = __ballot_sync(0xffffffffu, kp);
-            if (kp) kept[out + __popc(km & lt)] = r;
+            if (kp) kept[out + __popc(km & lt)] = row0 + r;
             out += __popc(km);
             eqr += __popc(em);
         }
@@ -1657,8 +1678,28 @@ __device__ __forceinline__ int ordered_keep(int n, uint32_t T, int allow, int32_
     return gt_all + min(eq_all, al);
 }
 
-/* Keys of up to SELECT_SMEM_KEYS rows fit in a k_select<*, true> block's
- * shared memory (with the 16 KB histogram): one block per SM, 1024 threads. */
+/* Kept-count totals of a block that owns all of a unit's rows: (gt, eq)
+ * before it, (gt, eq) over the unit. */
+struct SoloTotals {
+    __device__ int4 operator()(int gt, int eq) const { return make_int4(0, 0, gt, eq); }
+};
+
+/* Writes, in row order, the rows r < n whose key(r) > T, and the first
+ * `allow` rows whose key(r) == T, to kept[]; returns how many.  Each warp
+ * takes a contiguous range of rows, 32 at a time, so the counting is two
+ * ballots per 32 rows, the only block-wide step is one exchange of the warps'
+ * counts, and the indices go out as coalesced stores. */
+template <class KeyOf>
+__device__ __forceinline__ int ordered_keep(int n, uint32_t T, int allow, int32_t *kept, KeyOf key) {
+    __shared__ int s_gt[32], s_eq[32];
+    ordered_counts(n, T, key, s_gt, s_eq);
+    __syncthreads();
+    return ordered_write(n, T, allow, kept, key, 0, s_gt, s_eq, SoloTotals());
+}
+
+/* Keys of up to SELECT_SMEM_KEYS rows fit in the shared memory of a
+ * k_select<*, true> block or a k_select_cl CTA (with their histograms): one
+ * CTA per SM, 1024 threads. */
 constexpr int SELECT_SMEM_KEYS = 48 * 1024;
 constexpr int SELECT_BLOCK_SM = 1024;
 
@@ -1787,10 +1828,10 @@ __device__ __forceinline__ void select_unit(const SelectArgs &a, int u, uint32_t
     if (tid == 0) a.n_kept[u] = kept_n;
 }
 
-/* SMK: the unit's keys live in dynamic shared memory (n <= SELECT_SMEM_KEYS),
- * so the radix passes and the ordered output never leave the SM; else in
- * a.keys (global).  Either way the first digit's histogram is built in the
- * key pass. */
+/* One block per unit.  SMK: the unit's keys live in dynamic shared memory
+ * (n <= SELECT_SMEM_KEYS), so the radix passes and the ordered output never
+ * leave the SM; else in a.keys (global).  Either way the first digit's
+ * histogram is built in the key pass. */
 template <bool FUSED, bool SMK>
 __global__ void __launch_bounds__(SMK ? SELECT_BLOCK_SM : SELECT_BLOCK, SMK ? 1 : 2) k_select(const SelectArgs a) {
     __shared__ int s_hist[4096];
@@ -1801,6 +1842,199 @@ __global__ void __launch_bounds__(SMK ? SELECT_BLOCK_SM : SELECT_BLOCK, SMK ? 1 
     const int u = blockIdx.x;
     if (FUSED && (int)threadIdx.x < a.G) s_zs[threadIdx.x] = a.ms[(int64_t)u * a.G + threadIdx.x];
     select_unit<FUSED>(a, u, SMK ? s_keys : a.keys + (int64_t)u * a.key_stride, s_zs, s_hist, s_warp, s_bc);
+}
+
+/* Kept-count totals over the CTAs of a cluster that split one unit's rows in
+ * rank order: each CTA publishes its block totals, and reads every rank's
+ * through distributed shared memory after a cluster barrier. */
+struct ClusterTotals {
+    int *s_tot;                                          /* [2] this CTA's (gt, eq) */
+    __device__ int4 operator()(int gt, int eq) const {
+        cooperative_groups::cluster_group cl = cooperative_groups::this_cluster();
+        if (threadIdx.x == 0) { s_tot[0] = gt; s_tot[1] = eq; }
+        cl.sync();
+        const int me = (int)cl.block_rank(), nr = (int)cl.num_blocks();
+        int gb = 0, eb = 0, ga = 0, ea = 0;
+        for (int rk = 0; rk < nr; rk++) {
+            const int *t = cl.map_shared_rank(s_tot, rk);
+            const int g = t[0], e = t[1];
+            if (rk < me) { gb += g; eb += e; }
+            ga += g;
+            ea += e;
+        }
+        return make_int4(gb, eb, ga, ea);
+    }
+};
+
+/* Rows per CTA when a unit of n rows is split over cl CTAs: a multiple of 32,
+ * so every CTA's first row keeps the raw rows' 16-byte alignment. */
+__host__ __device__ __forceinline__ int select_cl_chunk(int n, int cl) { return ((n + cl - 1) / cl + 31) & ~31; }
+
+/* Selection of one unit with its keys in shared memory by a cluster of CTAs
+ * (cluster size from the launch: a launch with fewer units than SMs splits
+ * each unit's rows over 2 CTAs).  Same result as select_unit.
+ *  - CTA `rank` keys rows [r0, r1) of the unit into its shared memory and
+ *    histograms their first (12-bit) digit; the radix passes histogram the
+ *    next digits of its keys that match the prefix so far.  The CTAs of a
+ *    cluster read each other's histograms through distributed shared memory
+ *    (one buffer per digit, so none is overwritten while another CTA may
+ *    read it), so all of them settle on the same threshold.
+ *  - The ordered output offsets each CTA's rows by the kept counts of the
+ *    CTAs before it. */
+template <bool FUSED>
+__global__ void __launch_bounds__(SELECT_BLOCK_SM, 1) k_select_cl(const SelectArgs a) {
+    __shared__ int s_h0[4096], s_h1[1024], s_h2[1024];
+    __shared__ int s_gt[32], s_eq[32];
+    __shared__ int s_warp[32];
+    __shared__ int s_bc[2];
+    __shared__ int s_tot[2];
+    __shared__ int s_prot;
+    __shared__ float2 s_zs[TRIA_MAX_GQA];
+    extern __shared__ __align__(16) uint32_t keys[];
+    cooperative_groups::cluster_group cl = cooperative_groups::this_cluster();
+    const int ncl = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+    const int tid = threadIdx.x, bd = blockDim.x;
+    const int u = blockIdx.x / ncl;
+    const int n = a.n_rows[u];
+    const int chunk = select_cl_chunk(n, ncl);
+    const int r0 = min(n, rank * chunk), r1 = min(n, r0 + chunk), m = r1 - r0;
+    int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
+    const bool prot_on = a.window > 0 || a.sink > 0;
+    /* a barrier over the unit's CTAs; shared memory of rank rk */
+    auto csync = [&]() {
+        if (ncl > 1) cl.sync();
+        else __syncthreads();
+    };
+    auto at_rank = [&](int *p, int rk) -> const int * { return ncl > 1 ? cl.map_shared_rank(p, rk) : p; };
+    if (FUSED && tid < a.G) s_zs[tid] = a.ms[(int64_t)u * a.G + tid];
+    for (int i = tid; i < 4096; i += bd) s_h0[i] = 0;
+    for (int i = tid; i < 1024; i += bd) { s_h1[i] = 0; s_h2[i] = 0; }
+    __syncthreads();
+
+    /* keys of rows [r0, r1), SB rows per thread in flight */
+    constexpr int SB = 8;
+    int prot = 0;
+    for (int rb = r0 + (FUSED ? 4 * tid : tid); rb < r1; rb += SB * bd) {
+        auto row_of = [&](int j) { return FUSED ? rb + (j & 3) + (j >> 2) * 4 * bd : rb + j * bd; };
+        float x[SB];
+#pragma unroll
+        for (int j = 0; j < SB; j++) x[j] = 0.f;
+        if constexpr (FUSED) {
+            /* z-score max over the group, as group_zmax (triattention.c:240-247) */
+            for (int g = 0; g < a.G; g++) {
+                const float *xr = a.raw + ((int64_t)u * a.G + g) * a.raw_stride;
+                const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 v0 = *reinterpret_cast<const float4 *>(xr + rb);
+                const float4 v1 = rb + 4 * bd < r1 ? *reinterpret_cast<const float4 *>(xr + rb + 4 * bd) : z4;
+                const float v[SB] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                const float2 ms = s_zs[g];
+#pragma unroll
+                for (int j = 0; j < SB; j++) {
+                    const float z = __fdiv_rn(__fsub_rn(v[j], ms.x), ms.y);
+                    if (g == 0 || z > x[j]) x[j] = z;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < SB; j++)
+                if (rb + j * bd < r1) x[j] = a.scores[(int64_t)u * a.score_stride + rb + j * bd];
+        }
+        int p[SB];
+#pragma unroll
+        for (int j = 0; j < SB; j++) {
+            const int r = row_of(j);
+            p[j] = prot_on && r < r1 ? a.pos[a.pos_shared ? (int64_t)r : (int64_t)u * a.pos_cells + r] : 0;
+        }
+#pragma unroll
+        for (int j = 0; j < SB; j++) {
+            const int r = row_of(j);
+            if (r >= r1) continue;
+            uint32_t k = score_key(x[j]);
+            if (prot_on && ((a.sink > 0 && p[j] < a.sink) || (a.window > 0 && p[j] >= a.cur_pos - a.window))) {
+                k = 0xffffffffu;
+                prot++;
+            }
+            keys[r - r0] = k;
+            atomicAdd(&s_h0[k >> 20], 1);
+        }
+    }
+    const int bp = prot_on ? block_sum(prot, s_warp) : 0;
+    if (tid == 0) s_prot = bp;
+    csync();                                             /* every CTA's keys, first histogram and count */
+    int n_prot = 0;
+    if (prot_on)
+        for (int rk = 0; rk < ncl; rk++) n_prot += *at_rank(&s_prot, rk);
+    int keep = a.keep_req[u] > n_prot ? a.keep_req[u] : n_prot;
+    keep = keep > n ? n : (keep < 0 ? 0 : keep);
+
+    if (keep == n || keep == 0) {                        /* identity, or nothing kept */
+        if (keep == n)
+            for (int r = r0 + tid; r < r1; r += bd) kept[r] = r;
+        if (rank == 0 && tid == 0) a.n_kept[u] = keep;
+        if (ncl > 1) cl.sync();                          /* no CTA leaves while its s_prot may be read */
+        return;
+    }
+
+    /* this thread's bins [tid*c, tid*c + c) of digit histogram h, summed over
+     * the unit's CTAs */
+    auto merged = [&](int *h, int nb) {
+        const int c = (nb + bd - 1) / bd;
+        int own = 0;
+        for (int rk = 0; rk < ncl; rk++) {
+            const int *hr = at_rank(h, rk);
+            for (int i = 0; i < c; i++) own += tid * c + i < nb ? hr[tid * c + i] : 0;
+        }
+        return own;
+    };
+    uint32_t prefix = 0;
+    int need = keep;
+    for (int pass = 0; pass < 3; pass++) {
+        const int shift = pass == 0 ? 20 : (pass == 1 ? 10 : 0);
+        const int nb = pass == 0 ? 4096 : 1024;
+        const int hi = shift + 10;
+        int *h = pass == 0 ? s_h0 : (pass == 1 ? s_h1 : s_h2);
+        if (pass > 0) {                                  /* this CTA's keys that match the prefix */
+            for (int rb = tid; rb < m; rb += 8 * bd) {
+                uint32_t kk[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) kk[j] = rb + j * bd < m ? keys[rb + j * bd] : 0u;
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    if (rb + j * bd < m && (kk[j] >> hi) == (prefix >> hi))
+                        atomicAdd(&h[(kk[j] >> shift) & (uint32_t)(nb - 1)], 1);
+            }
+            csync();
+        }
+        const int c = (nb + bd - 1) / bd;
+        const int own = merged(h, nb);
+        const int incl = block_suffix_sum(own, s_warp);
+        const int above = incl - own;
+        if (above < need && need <= incl) {
+            int acc = above;
+            for (int i = c - 1; i >= 0; i--) {
+                int hsum = 0;
+                if (tid * c + i < nb)
+                    for (int rk = 0; rk < ncl; rk++) hsum += at_rank(h, rk)[tid * c + i];
+                if (acc + hsum >= need) { s_bc[0] = tid * c + i; s_bc[1] = need - acc; break; }
+                acc += hsum;
+            }
+        }
+        __syncthreads();
+        prefix |= (uint32_t)s_bc[0] << shift;
+        need = s_bc[1];
+        __syncthreads();
+    }
+    /* keys above the threshold, and the first `need` equal to it in row order */
+    const uint32_t T = prefix;
+    ordered_counts(m, T, [&](int r) { return keys[r]; }, s_gt, s_eq);
+    __syncthreads();
+    int kept_n;
+    if (ncl > 1)
+        kept_n = ordered_write(m, T, need, kept, [&](int r) { return keys[r]; }, r0, s_gt, s_eq, ClusterTotals{s_tot});
+    else
+        kept_n = ordered_write(m, T, need, kept, [&](int r) { return keys[r]; }, 0, s_gt, s_eq, SoloTotals());
+    if (rank == 0 && tid == 0) a.n_kept[u] = kept_n;
+    if (ncl > 1) cl.sync();                              /* no CTA leaves while its shared memory may be read */
 }
 
 /* ------------------------------------------------------------------ */

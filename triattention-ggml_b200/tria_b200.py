@@ -195,6 +195,7 @@ def lib() -> C.CDLL:
         L.tria_ggml_evict.argtypes = [C.c_void_p, C.POINTER(GgmlCache), C.POINTER(GgmlCache), C.c_void_p,
                                       C.POINTER(EvictParams), C.c_void_p]
         L.tria_ctx_set_wait_limit.argtypes = [C.c_void_p, C.c_int64]
+        L.tria_ctx_set_select_split.argtypes = [C.c_void_p, C.c_int32]
         L.tria_select_noalloc.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int32,
                                           C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
                                           C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]
@@ -435,6 +436,10 @@ class Context:
     def set_wait_limit(self, cycles: int = 0):
         """tria_ctx_set_wait_limit (timeout-path tests): 0 restores the default."""
         check(lib().tria_ctx_set_wait_limit(self.h, int(cycles)))
+
+    def set_select_split(self, max_ctas: int = 0):
+        """tria_ctx_set_select_split: CTAs per unit in selection (0 automatic, 1 one block)."""
+        check(lib().tria_ctx_set_select_split(self.h, int(max_ctas)))
 
     def score_kv_head_dev(self, k_re, k_im, key_pos, cur_pos, n, layer, kv_head, out, stream=None):
         check(lib().tria_score_kv_head_dev(self.h, _ptr(k_re), _ptr(k_im), _ptr(key_pos), int(cur_pos),
