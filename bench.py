@@ -374,11 +374,15 @@ def run_ours(args):
     clk = clocks.summary()
     ms_max = max_over_ranks(ms)
 
-    # stage timing (CUDA events between stages, same workload)
+    # stage timing (CUDA events between stages, same workload).  Two steps are
+    # queued back to back and the second one's events are read: reading them
+    # waits for the step, so a step queued after a read would start on an
+    # idle GPU and its first stages would include the host's launch time.
     ctx.set_timing(True)
     acc = {}
     with torch.cuda.stream(stream):
         for _ in range(max(3, min(args.steps, 50))):
+            ctx.evict(sv, dv, n_rows, params, stream=stream)
             ctx.evict(sv, dv, n_rows, params, stream=stream)
             for k, v in ctx.stage_ms().items():
                 acc.setdefault(k, []).append(v)
@@ -608,6 +612,7 @@ def run_ramp(args):
         for t in range(T):
             acc = {}
             for _ in range(5):
+                step(t)                 # queued ahead: the timed step below starts on a busy GPU
                 step(t)
                 for k, v in ctx.stage_ms().items():
                     acc.setdefault(k, []).append(v)
