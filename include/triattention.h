@@ -113,7 +113,9 @@ enum tria_status {
     TRIA_ERR_POSITION    = -4,  /* a key position lies outside [0, cur_pos] */
     TRIA_ERR_UNSUPPORTED = -5,  /* geometry or cache type not supported */
     TRIA_ERR_NO_DEVICE   = -6,  /* no CUDA device / not an sm_100 device */
-    TRIA_ERR_TIMEOUT     = -7   /* a bounded wait inside a kernel gave up; that step's output is undefined */
+    TRIA_ERR_TIMEOUT     = -7,  /* a bounded wait inside a kernel gave up; that step's output is undefined */
+    TRIA_ERR_BOUNDS      = -8   /* checked build only: an index or extent was out of range; the access was
+                                   skipped and that step's output is undefined */
 };
 
 /* Cache element types (ggml type ids). */
@@ -272,6 +274,14 @@ TRIA_API int tria_ctx_check(tria_ctx *ctx, void *stream);
  * restores the default.  A step that timed out reports TRIA_ERR_TIMEOUT from
  * tria_get_n_kv / tria_ctx_check and leaves the context usable. */
 TRIA_API int tria_ctx_set_wait_limit(tria_ctx *ctx, int64_t cycles);
+
+/* 1 in the checked build (libtriattention_b200_checked.so, `make checked`),
+ * 0 in the product library.  The checked build's kernels test every index
+ * and extent that comes from device data or from the call (kept indices and
+ * counts, row counts against the buffers' strides, source cell ranges, raw
+ * score writes) and report a failure as TRIA_ERR_BOUNDS instead of touching
+ * memory out of range.  New; no reference counterpart. */
+TRIA_API int tria_checked_build(void);
 
 /* Tuning: the most CTAs that selection may give one (layer, kv-head) unit
  * (up to 8).  0, the default, lets the library split a unit over a

@@ -28,6 +28,18 @@ def test_exports_every_header_symbol(L):
         assert hasattr(L, n), n
 
 
+def test_checked_build_exports_the_same_symbols(L):
+    """The checked build (make checked) is the same ABI with bounds checks in
+    its kernels; it says so through tria_checked_build, the product does not."""
+    if not os.path.exists(tria_b200.CHECKED_LIB_PATH):
+        tria_b200.build()
+    CL = C.CDLL(tria_b200.CHECKED_LIB_PATH)
+    for n in tria_b200.exported_symbols_in_header():
+        assert hasattr(CL, n), n
+    assert CL.tria_checked_build() == 1
+    assert L.tria_checked_build() == (1 if tria_b200.LIB_PATH == tria_b200.CHECKED_LIB_PATH else 0)
+
+
 def test_no_oracle_or_reference_symbols_in_product(L):
     """The product never links the checker."""
     for n in ("oracle_score_kv_head", "oracle_select", "score_keys", "tria_score_ref_main"):

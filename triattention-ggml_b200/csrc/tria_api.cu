@@ -69,6 +69,7 @@ extern "C" TRIA_API const char *tria_status_str(int st) {
         case TRIA_ERR_UNSUPPORTED: return "unsupported geometry";
         case TRIA_ERR_NO_DEVICE: return "no sm_100 CUDA device";
         case TRIA_ERR_TIMEOUT: return "a bounded wait inside a kernel gave up";
+        case TRIA_ERR_BOUNDS: return "a bounds check of the checked build failed";
         default: return "unknown status";
     }
 }
@@ -99,6 +100,9 @@ static int status_of_bits(int32_t bits, const char *what) {
     if (bits & ST_POSITION)
         FAIL(TRIA_ERR_POSITION, "%s: a key position was outside [0, cur_pos] (status 0x%x); "
              "that step's output is undefined", what, bits);
+    if (bits & ST_BOUNDS)
+        FAIL(TRIA_ERR_BOUNDS, "%s: a bounds check of the checked build failed (status 0x%x): an index or "
+             "extent from the device or the call was out of range and that access was skipped", what, bits);
     FAIL(TRIA_ERR_CUDA, "%s: unknown kernel status bits 0x%x", what, bits);
 }
 
@@ -483,6 +487,7 @@ static int launch_znorm(tria_ctx *c, int64_t unit0, int units, const int32_t *n_
     z.G = (int32_t)c->G;
     z.units = units;
     z.ms = c->ms + unit0 * c->G;
+    z.status = c->d_status;
     for (int u = 0; u < units; u++) z.n_rows[u] = n_rows[unit0 + u];
     CUDA_TRY(launch_znorm_chains(z, units * (int)c->G, c->sm_count, st));
     c->launches++;
@@ -751,6 +756,7 @@ static int launch_select(tria_ctx *c, const tria_kv_view *v, const int32_t *n_ro
         a->kept_idx = kept_idx + u0 * kept_stride;
         a->kept_stride = kept_stride;
         a->n_kept = n_kept + u0;
+        a->status = c->d_status;
         for (int u = 0; u < units; u++) {
             a->n_rows[u] = n_rows[u0 + u];
             a->keep_req[u] = keep[u0 + u];
@@ -836,6 +842,10 @@ static int launch_compact(tria_ctx *c, const tria_kv_view *s, const tria_kv_view
         a->n_head_kv = s->n_head_kv;
         a->row_bytes = (int32_t)rb;
         a->has_v = s->v ? 1 : 0;
+        a->status = c->d_status;
+#ifdef TRIA_CHECKS
+        for (int u = 0; u < units; u++) a->n_rows[u] = n_rows[u0 + u];
+#endif
         int max_rows = 0;
         for (int u = 0; u < units; u++) max_rows = std::max(max_rows, n_rows[u0 + u]);
         const int rows = rows_hint >= 0 ? std::min(rows_hint, max_rows) : max_rows;
@@ -1053,6 +1063,7 @@ extern "C" TRIA_API int tria_znorm_stats(const float *x, int64_t stride, const i
         z.G = 1;
         z.units = cn;
         z.ms = reinterpret_cast<float2 *>(mean_std) + c0;
+        z.status = nullptr;                 /* no context: the extents are checked above */
         for (int i = 0; i < cn; i++) z.n_rows[i] = n[c0 + i];
         int dev = 0, sms = 148;
         if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -1375,6 +1386,14 @@ extern "C" TRIA_API int tria_ctx_check(tria_ctx *c, void *stream) {
     CUDA_TRY(cudaMemsetAsync(c->d_status, 0, 4, st));
     CUDA_TRY(cudaStreamSynchronize(st));
     return status_of_bits(bits, "tria_ctx_check");
+}
+
+extern "C" TRIA_API int tria_checked_build(void) {
+#ifdef TRIA_CHECKS
+    return 1;
+#else
+    return 0;
+#endif
 }
 
 extern "C" TRIA_API int tria_ctx_set_select_split(tria_ctx *c, int32_t max_ctas) {

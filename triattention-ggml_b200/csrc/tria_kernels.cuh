@@ -51,7 +51,26 @@ enum : int { KT_F32SPLIT = 0, KT_F16 = TRIA_TYPE_F16, KT_Q8_0 = TRIA_TYPE_Q8_0 }
 /* Bits of the device status word (tria_ctx's d_status), decoded on the host
  * by tria_status_of_bits(): a key position outside the table, a bounded
  * pipeline wait that gave up. */
-enum : int { ST_POSITION = 1, ST_TIMEOUT = 2 };
+enum : int { ST_POSITION = 1, ST_TIMEOUT = 2, ST_BOUNDS = 4 };
+
+/* Bounds checks of the checked build (compiled with TRIA_CHECKS): a failed
+ * check sets ST_BOUNDS in *status and the caller skips the access.  In the
+ * product build the check is the constant true and compiles away. */
+__device__ __forceinline__ uint32_t dynamic_smem_bytes() {
+    uint32_t b;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(b));
+    return b;
+}
+__device__ __forceinline__ bool bounds_ok(bool ok, int32_t *status) {
+#ifdef TRIA_CHECKS
+    if (!ok && status) atomicOr(status, ST_BOUNDS);
+    return ok;
+#else
+    (void)ok;
+    (void)status;
+    return true;
+#endif
+}
 
 constexpr int N_OFF = 17;
 constexpr int SCORE_THREADS = 256;
@@ -763,7 +782,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
             int l, c0;
             const int cells = item_of(kk, l, c0);
             uint64_t *bar = &posbar[kk % WS_POS_RING];
-            const int nrow = cells == 0 ? 0 : (a.pos_shared ? 1 : KV);
+            const bool inb = bounds_ok(c0 + cells <= a.n_cells, lane == 0 ? a.status : nullptr);
+            const int nrow = cells == 0 || !inb ? 0 : (a.pos_shared ? 1 : KV);
             const uint32_t pb = (uint32_t)((cells + 3) / 4 * 16);   /* whole 16-byte groups (n_cells % 4 == 0) */
             if (lane == 0) mbar_arrive_tx(bar, pb * nrow);
             __syncwarp();
@@ -834,7 +854,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                 if (lane == 0 && __popc(okm) != cells) atomicOr(a.status, ST_POSITION);
                 __syncwarp();
             }
-            if (lane == 0 && cells > 0) {
+            if (lane == 0 && cells > 0 && bounds_ok(c0 + cells <= a.n_cells, a.status)) {
                 mbar_expect(&full[st], (uint32_t)(cells * a.cell_stride));
                 bulk_g2s(sb, a.k[l] + (int64_t)c0 * a.cell_stride, (uint32_t)(cells * a.cell_stride), &full[st]);
             }
@@ -882,6 +902,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_score_ws(const TmaScoreArgs a
                 const int h = r / SC_T, c = r - h * SC_T;
                 const int u = l * KV + h;
                 if (c >= min(cells, a.n_rows[u] - c0)) continue;
+                if (!bounds_ok(c0 + c < a.raw_stride, a.status)) continue;
                 const float *row = pb + r * 8 * LP;
                 float sum[8];
 #pragma unroll
@@ -963,6 +984,7 @@ struct ZArgs {
     int64_t raw_stride;                  /* floats, multiple of 4 */
     int32_t G, units;
     float2 *ms;                          /* [units*G] (mean, std) */
+    int32_t *status;                     /* ST_BOUNDS of the checked build (may be null in the product) */
     int32_t n_rows[TRIA_MAX_UNITS];
 };
 
@@ -1264,7 +1286,8 @@ __global__ void __launch_bounds__(ZS_WARPS * 32, 8) k_znorm_seg(const ZArgs a) {
     __shared__ __align__(16) float s_vals[ZS_WIN * ZS_SEG];
     __shared__ float s_state;
     const int t = blockIdx.x;
-    const int n = a.n_rows[t / a.G];
+    int n = a.n_rows[t / a.G];
+    if (!bounds_ok(n >= 0 && n <= a.raw_stride, a.status)) n = 0;
     const float *x = a.raw + (int64_t)t * a.raw_stride;
     const float sum = zs_pass(x, n, [](float v) { return v; }, s_sum, s_rec, s_vals, &s_state);
     const float mean = __fdiv_rn(sum, (float)n);
@@ -1466,7 +1489,8 @@ __global__ void __launch_bounds__(ZP_WARPS * 32, 2) k_znorm_pre(const ZArgs a) {
     __shared__ float s_state;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int t = blockIdx.x;
-    const int n = a.n_rows[t / a.G];
+    int n = a.n_rows[t / a.G];
+    if (!bounds_ok(n >= 0 && n <= a.raw_stride && (n + ZS_SEG - 1) / ZS_SEG <= ZP_MAX_SEG, a.status)) n = 0;
     const float *x = a.raw + (int64_t)t * a.raw_stride;
     const int nseg = (n + ZS_SEG - 1) / ZS_SEG;
     ZpSmem S;                                          /* 16-byte pieces first: staging, records */
@@ -1571,6 +1595,7 @@ struct SelectArgs {
     int32_t *kept_idx;
     int64_t kept_stride;
     int32_t *n_kept;
+    int32_t *status;                  /* ST_BOUNDS of the checked build */
     int32_t n_rows[TRIA_MAX_UNITS];
     int32_t keep_req[TRIA_MAX_UNITS];
 };
@@ -1703,17 +1728,27 @@ __device__ __forceinline__ int ordered_keep(int n, uint32_t T, int allow, int32_
 constexpr int SELECT_SMEM_KEYS = 48 * 1024;
 constexpr int SELECT_BLOCK_SM = 1024;
 
+/* A unit of n rows against the extents its selection reads and writes: the
+ * key array (key_cap entries), the kept-index row, the positions (window /
+ * sink; pos_cells 0 when the caller gave no extent) and the raw or final
+ * score row. */
+__device__ __forceinline__ bool select_rows_ok(const SelectArgs &a, int n, int64_t key_cap, bool fused, bool prot_on) {
+    return n >= 0 && n <= key_cap && n <= a.kept_stride && (!prot_on || a.pos_cells <= 0 || n <= a.pos_cells) &&
+           n <= (fused ? a.raw_stride : a.score_stride);
+}
+
 /* Selection of unit u by the whole block: keys (in `keys`, shared or global
  * memory), radix select, ordered output.  FUSED: keys from the raw scores and
  * the (mean, std) of the unit's query heads in s_zs (shared); else from
  * a.scores.  s_hist is the block's [4096] histogram. */
 template <bool FUSED>
-__device__ __forceinline__ void select_unit(const SelectArgs &a, int u, uint32_t *keys, const float2 *s_zs,
-                                            int *s_hist, int *s_warp, int *s_bc) {
+__device__ __forceinline__ void select_unit(const SelectArgs &a, int u, uint32_t *keys, int64_t key_cap,
+                                            const float2 *s_zs, int *s_hist, int *s_warp, int *s_bc) {
     const int tid = threadIdx.x, bd = blockDim.x;
-    const int n = a.n_rows[u];
-    int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
     const bool prot_on = a.window > 0 || a.sink > 0;
+    int n = a.n_rows[u];
+    if (!bounds_ok(select_rows_ok(a, n, key_cap, FUSED, prot_on), tid == 0 ? a.status : nullptr)) n = 0;
+    int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
     for (int i = tid; i < 4096; i += bd) s_hist[i] = 0;
     __syncthreads();
     /* keys, SB rows per thread in flight (the raw scores are L2 / DRAM round
@@ -1841,7 +1876,8 @@ __global__ void __launch_bounds__(SMK ? SELECT_BLOCK_SM : SELECT_BLOCK, SMK ? 1 
     extern __shared__ __align__(16) uint32_t s_keys[];
     const int u = blockIdx.x;
     if (FUSED && (int)threadIdx.x < a.G) s_zs[threadIdx.x] = a.ms[(int64_t)u * a.G + threadIdx.x];
-    select_unit<FUSED>(a, u, SMK ? s_keys : a.keys + (int64_t)u * a.key_stride, s_zs, s_hist, s_warp, s_bc);
+    select_unit<FUSED>(a, u, SMK ? s_keys : a.keys + (int64_t)u * a.key_stride,
+                       SMK ? (int64_t)(dynamic_smem_bytes() / 4) : a.key_stride, s_zs, s_hist, s_warp, s_bc);
 }
 
 /* Kept-count totals over the CTAs of a cluster that split one unit's rows in
@@ -1895,11 +1931,15 @@ __global__ void __launch_bounds__(SELECT_BLOCK_SM, 1) k_select_cl(const SelectAr
     const int ncl = (int)cl.num_blocks(), rank = (int)cl.block_rank();
     const int tid = threadIdx.x, bd = blockDim.x;
     const int u = blockIdx.x / ncl;
-    const int n = a.n_rows[u];
+    const bool prot_on = a.window > 0 || a.sink > 0;
+    int n = a.n_rows[u];
+    if (!bounds_ok(select_rows_ok(a, n, (int64_t)ncl * (dynamic_smem_bytes() / 4), FUSED, prot_on) &&
+                       select_cl_chunk(n, ncl) <= (int)(dynamic_smem_bytes() / 4),
+                   tid == 0 && rank == 0 ? a.status : nullptr))
+        n = 0;
     const int chunk = select_cl_chunk(n, ncl);
     const int r0 = min(n, rank * chunk), r1 = min(n, r0 + chunk), m = r1 - r0;
     int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
-    const bool prot_on = a.window > 0 || a.sink > 0;
     /* a barrier over the unit's CTAs; shared memory of rank rk */
     auto csync = [&]() {
         if (ncl > 1) cl.sync();
@@ -2157,7 +2197,34 @@ struct CompactArgs {
     int64_t kept_stride;
     const int32_t *n_kept;
     int32_t n_head_kv, row_bytes, has_v;
+    int32_t *status;                  /* ST_BOUNDS of the checked build */
+#ifdef TRIA_CHECKS
+    int32_t n_rows[TRIA_MAX_UNITS];   /* source rows of each unit: the kept indices' bound */
+#endif
 };
+
+/* Kept count of unit u; the checked build holds it to the unit's source rows
+ * and the destination's cells. */
+__device__ __forceinline__ int compact_count(const CompactArgs &a, int u) {
+    int nk = a.n_kept[u];
+#ifdef TRIA_CHECKS
+    const int lim = min(a.n_rows[u], a.cells_d);
+    if (!bounds_ok(nk >= 0 && nk <= lim, threadIdx.x == 0 ? a.status : nullptr)) nk = max(0, min(nk, lim));
+#endif
+    return nk;
+}
+
+/* Kept index r of unit u: the checked build requires a source row. */
+__device__ __forceinline__ bool compact_row_ok(const CompactArgs &a, int u, int r) {
+#ifdef TRIA_CHECKS
+    return bounds_ok(r >= 0 && r < a.n_rows[u], a.status);
+#else
+    (void)a;
+    (void)u;
+    (void)r;
+    return true;
+#endif
+}
 
 template <int VEC>
 struct VecT;
@@ -2170,7 +2237,7 @@ __global__ void __launch_bounds__(256) k_compact(const CompactArgs a) {
     using V = typename VecT<VEC>::T;
     const int u = blockIdx.y;
     const int l = u / a.n_head_kv, h = u - l * a.n_head_kv;
-    const int nk = a.n_kept[u];
+    const int nk = compact_count(a, u);
     const int chunks = a.row_bytes / VEC;
     const int64_t total = (int64_t)nk * chunks;
     const int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
@@ -2183,6 +2250,7 @@ __global__ void __launch_bounds__(256) k_compact(const CompactArgs a) {
         const int jrow = (int)(i / chunks);
         const int c = (int)(i - (int64_t)jrow * chunks);
         const int r = kept[jrow];
+        if (!compact_row_ok(a, u, r)) continue;
         const V kv = *reinterpret_cast<const V *>(ks + (int64_t)r * a.cs_s + c * VEC);
         *reinterpret_cast<V *>(kd + (int64_t)jrow * a.cs_d + c * VEC) = kv;
         if (vs) {
@@ -2205,7 +2273,7 @@ __global__ void __launch_bounds__(256) k_compact_rows(const CompactArgs a) {
     constexpr int RPW = 32 / CH;
     const int u = blockIdx.y;
     const int l = u / a.n_head_kv, h = u - l * a.n_head_kv;
-    const int nk = a.n_kept[u];
+    const int nk = compact_count(a, u);
     const int lane = threadIdx.x & 31, c = lane % CH, sub = lane / CH;
     const int32_t *kept = a.kept_idx + (int64_t)u * a.kept_stride;
     const uint8_t *ks = a.ks[l] + (int64_t)h * a.hs_s;
@@ -2220,6 +2288,7 @@ __global__ void __launch_bounds__(256) k_compact_rows(const CompactArgs a) {
         for (int q = 0; q < 2; q++) {
             jr[q] = (int)(jb + q * RPW + sub);
             rr[q] = jr[q] < nk ? kept[jr[q]] : 0;
+            if (jr[q] < nk && !compact_row_ok(a, u, rr[q])) jr[q] = nk;      /* skipped */
         }
         uint4 kv[2], vv[2];
 #pragma unroll
@@ -2254,15 +2323,16 @@ __global__ void __launch_bounds__(256) k_compact_split(const CompactArgs a) {
     const int nch = a.row_bytes / 16;
     const int lane = threadIdx.x & 31, c = lane & 7, sub = lane >> 3;
     int nk_max = 0;
-    for (int h = 0; h < KV; h++) nk_max = max(nk_max, a.n_kept[l * KV + h]);
+    for (int h = 0; h < KV; h++) nk_max = max(nk_max, compact_count(a, l * KV + h));
     const int64_t wg = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t j = wg; j < nk_max; j += nw) {
         const int jr = (int)j;
         for (int h0 = 0; h0 < KV; h0 += 4) {
             const int h = h0 + sub, u = l * KV + h;
-            if (h >= KV || jr >= a.n_kept[u]) continue;
+            if (h >= KV || jr >= compact_count(a, u)) continue;
             const int r = a.kept_idx[(int64_t)u * a.kept_stride + jr];
+            if (!compact_row_ok(a, u, r)) continue;
             const bool lead8 = (((int64_t)h * a.hs_s) & 15) != 0;
             const int off16 = (lead8 ? 8 : 0) + 16 * c, off8 = lead8 ? 0 : a.row_bytes - 8;
             const int64_t so = (int64_t)r * a.cs_s + (int64_t)h * a.hs_s, d0 = (int64_t)jr * a.cs_d + (int64_t)h * a.hs_d;

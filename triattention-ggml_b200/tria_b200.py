@@ -23,7 +23,11 @@ import subprocess
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libtriattention_b200.so")
+CHECKED_LIB_PATH = os.path.join(HERE, "libtriattention_b200_checked.so")
+# TRIA_B200_LIB=checked loads the checked build (bounds checks in every kernel,
+# TRIA_ERR_BOUNDS) instead of the product library
+LIB_PATH = CHECKED_LIB_PATH if os.environ.get("TRIA_B200_LIB") == "checked" else \
+    os.path.join(HERE, "libtriattention_b200.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "triattention.h")
 HEADERS = [HEADER, os.path.join(os.path.dirname(HERE), "include", "triattention_ggml.h")]
 
@@ -38,6 +42,7 @@ ERR_POSITION = -4
 ERR_UNSUPPORTED = -5
 ERR_NO_DEVICE = -6
 ERR_TIMEOUT = -7
+ERR_BOUNDS = -8
 
 
 class TriaError(RuntimeError):
@@ -152,8 +157,8 @@ def n_kv_per_seq(n_kept, seq_of_unit, n_seq):
 
 
 def build() -> str:
-    """Compile the library in-tree (nvcc, sm_100a)."""
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    """Compile the library (and the checked build) in-tree (nvcc, sm_100a)."""
+    subprocess.run(["make", "-s", "-C", HERE, "all", "checked"], check=True)
     return LIB_PATH
 
 
@@ -196,6 +201,7 @@ def lib() -> C.CDLL:
                                       C.POINTER(EvictParams), C.c_void_p]
         L.tria_ctx_set_wait_limit.argtypes = [C.c_void_p, C.c_int64]
         L.tria_ctx_set_select_split.argtypes = [C.c_void_p, C.c_int32]
+        L.tria_checked_build.argtypes = []
         L.tria_select_noalloc.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int32,
                                           C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
                                           C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]
@@ -278,6 +284,11 @@ def znorm_stats(x, stride, n, mean_std, stream=None):
     nn = np.ascontiguousarray(n, np.int32)
     check(lib().tria_znorm_stats(_ptr(x), int(stride), nn.ctypes.data, int(nn.shape[0]),
                                  _ptr(mean_std), _stream(stream)))
+
+
+def checked_build() -> bool:
+    """tria_checked_build: True when the loaded library is the checked build."""
+    return bool(lib().tria_checked_build())
 
 
 def score_key(x: float) -> int:
