@@ -8,6 +8,7 @@
  * kernels on host buffers through a context cached per (stats, device).
  */
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <cmath>
@@ -24,6 +25,29 @@
 #include "tria_kernels.cuh"
 
 using namespace tria;
+
+/* NVTX ranges on the host timeline (a profiler shows them beside the
+ * kernels; ncu --nvtx filters launches by them): a call, and the stages of an
+ * eviction step.  With no tool attached a push or pop is a branch. */
+struct NvtxRange {
+    explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange &) = delete;
+    NvtxRange &operator=(const NvtxRange &) = delete;
+};
+struct NvtxStages {
+    bool open = false;
+    void next(const char *name) {
+        close();
+        nvtxRangePushA(name);
+        open = true;
+    }
+    void close() {
+        if (open) nvtxRangePop();
+        open = false;
+    }
+    ~NvtxStages() { close(); }
+};
 
 /* Raises a kernel's dynamic shared-memory limit on the current device to at
  * least `bytes`.  The attribute belongs to each device's copy of the kernel
@@ -919,6 +943,7 @@ static int ensure_ptab(tria_ctx *c, int32_t cur_pos, cudaStream_t st) {
 
 extern "C" TRIA_API int tria_score(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, int32_t cur_pos,
                                    float *scores, void *stream) {
+    NvtxRange range("tria_score");
     if (!c || !n_rows || !scores) FAIL(TRIA_ERR_INVALID, "tria_score: null argument");
     int rc = validate_view(c, v, n_rows, "tria_score", false);
     if (rc) return rc;
@@ -950,6 +975,7 @@ extern "C" TRIA_API int tria_score(tria_ctx *c, const tria_kv_view *v, const int
 
 extern "C" TRIA_API int tria_select(tria_ctx *c, const tria_kv_view *v, const int32_t *n_rows, const float *scores,
                                     const tria_evict_params *p, int32_t *kept_idx, int32_t *n_kept, void *stream) {
+    NvtxRange range("tria_select");
     if (!c || !n_rows || !scores || !p || !kept_idx || !n_kept) FAIL(TRIA_ERR_INVALID, "tria_select: null argument");
     int rc = validate_view(c, v, n_rows, "tria_select", false);
     if (rc) return rc;
@@ -972,6 +998,7 @@ static int check_pair(const tria_kv_view *s, const tria_kv_view *d) {
 
 extern "C" TRIA_API int tria_compact(tria_ctx *c, const tria_kv_view *s, const tria_kv_view *d, const int32_t *n_rows,
                                      const int32_t *kept_idx, const int32_t *n_kept, void *stream) {
+    NvtxRange range("tria_compact");
     if (!c || !n_rows || !kept_idx || !n_kept) FAIL(TRIA_ERR_INVALID, "tria_compact: null argument");
     int rc = validate_view(c, s, n_rows, "tria_compact src", false);
     if (!rc) rc = validate_view(c, d, nullptr, "tria_compact dst", false);
@@ -1003,7 +1030,12 @@ extern "C" TRIA_API int tria_evict(tria_ctx *c, const tria_kv_view *s, const tri
     std::vector<int32_t> keep;
     keep_requests(c, s, n_rows, p, keep);
     int32_t *cnt = n_kept_out ? n_kept_out : c->cnt;
+    NvtxRange step_range("tria_evict");
+    NvtxStages nv;
+    static const char *const stage_names[5] = {"table", "score", "znorm", "select", "compact"};
     auto stage = [&](int i) -> int {
+        if (i < 5) nv.next(stage_names[i]);
+        else nv.close();
         if (c->timing) CUDA_TRY(cudaEventRecord(c->ev_stage[i], st));
         return TRIA_OK;
     };
@@ -1103,6 +1135,7 @@ static int check_range(const void *base, size_t bytes, const char *what, int l) 
 
 extern "C" TRIA_API int tria_evict_host(tria_ctx *c, const tria_kv_view *s, const tria_kv_view *d,
                                         const int32_t *n_rows, const tria_evict_params *p, void *stream) {
+    NvtxRange range("tria_evict_host");
     if (!c || !n_rows || !p) FAIL(TRIA_ERR_INVALID, "tria_evict_host: null argument");
     int rc = validate_view(c, s, n_rows, "tria_evict_host src", false);
     if (!rc) rc = validate_view(c, d, nullptr, "tria_evict_host dst", false);
