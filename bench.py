@@ -732,11 +732,13 @@ def run_global(args):
         return torch.stack(out)
 
     backend = gbud.DeviceBackend(dev, stream)
+    one = args.global_protocol == "candidates"
+    select = gbud.global_select_candidates if one else gbud.global_select
 
     def step():
         for q in range(n_seq):
             ctx.score(views[q], n_rows[q], int(n_kv[q]), seqs[q]["scores"], stream=stream)
-        gbud.global_select(seqs, k_total, gather, backend, rank)
+        select(seqs, k_total, gather, backend, rank)
         for q in range(n_seq):
             ctx.compact(views[q], dviews[q], n_rows[q], seqs[q]["kept_idx"], seqs[q]["n_kept"], stream=stream)
 
@@ -788,7 +790,8 @@ def run_global(args):
                                f"n_kv {n_kv.tolist()}, head_dim {hd}, q8_0 K/V, global budget "
                                f"{c['budget']} rows per (layer, kv-head) per sequence",
                    "kept_rows": kept_total, "shard": f"contiguous layer blocks over {world} rank(s)",
-                   "collectives": "3 all-gathers of per-sequence key histograms / tie counts per step",
+                   "collectives": ("1 all-gather of per-sequence candidate scores per step" if one else
+                                   "3 all-gathers of per-sequence key histograms / tie counts per step"),
                    "l2": "inputs larger than L2 (no flush)"},
         "step_roofline": {"bytes_per_step": step_b, "achieved": step_b / (ms / 1e3) / 1e9,
                           "frac": step_b / (ms / 1e3) / 1e9 / peak, "unit": "GB/s",
@@ -809,6 +812,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
+    ap.add_argument("--global-protocol", default="histograms", choices=["histograms", "candidates"],
+                    help="multiseq-q8_0-global: three all-gathers of key histograms, or one of candidates")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
                     help="N > 1: strong (default) = layers partitioned over the ranks; weak = a full cache per rank")

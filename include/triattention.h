@@ -398,6 +398,18 @@ TRIA_API int tria_select_key(const float *scores, int64_t score_stride, const in
                              int32_t units, uint32_t key, const int32_t *counts, int64_t tie_allow,
                              int32_t *kept_idx, int64_t kept_stride, int32_t *n_kept, void *stream);
 
+/* For a single exchange between the ranks: the scores of every unit whose
+ * key is at least key_min, written to out[0..cap) in no particular order;
+ * *count (device int32, zeroed here) gets how many there were, also when
+ * that is more than cap.  A rank that gathers its rows at or above its own
+ * K-th largest key holds every row of the global top K (the global K-th key
+ * is never below a rank's own), ties at its own K-th key included, so one
+ * all-gather of these candidates lets every rank find the threshold and its
+ * share of the ties with steps 1-3 run on the gathered scores. */
+TRIA_API int tria_key_gather(const float *scores, int64_t score_stride, const int32_t *n_rows,
+                             int32_t units, uint32_t key_min, float *out, int32_t cap, int32_t *count,
+                             void *stream);
+
 #ifdef __cplusplus
 }
 #endif

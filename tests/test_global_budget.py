@@ -1,10 +1,11 @@
 """Global budget across units (multi-sequence serving), host logic on CPU.
 
 The orchestration in global_budget.py is run against a CPU stand-in for the
-three device calls (histogram, key count, select by key), in one process and
-on two gloo ranks that each own a contiguous block of layers; the kept sets
-must equal the oracle's global top-k with the (key desc, unit asc, row asc)
-rule, ties and NaN included.
+device calls (histogram, key count, select by key, key gather), in one
+process and on two gloo ranks that each own a contiguous block of layers,
+for both exchange protocols (three all-gathers, and one all-gather of
+candidates with its fallback); the kept sets must equal the oracle's global
+top-k with the (key desc, unit asc, row asc) rule, ties and NaN included.
 """
 import os
 import socket
@@ -35,6 +36,43 @@ class CpuBackend:
         import torch
         seq["_counts"] = np.array([int((np.asarray(k, np.uint32) == key).sum()) for k in seq["keys"]], np.int64)
         return torch.from_numpy(seq["_counts"])
+
+    def histograms(self, seqs, level, prefixes):
+        import torch
+        return torch.stack([self.histogram(sq, level, p) for sq, p in zip(seqs, prefixes)])
+
+    def rows(self, seq):
+        return int(sum(len(k) for k in seq["keys"]))
+
+    def candidates(self, seqs, key_mins, cap):
+        """[n_seq, CAND_HEAD + cap] int64: the count, then the keys >= key_mins[s]."""
+        import torch
+        buf = np.zeros((len(seqs), gb.CAND_HEAD + cap), np.int64)
+        for s, (sq, km) in enumerate(zip(seqs, key_mins)):
+            c = np.concatenate([np.asarray(k, np.uint32) for k in sq["keys"]] + [np.zeros(0, np.uint32)])
+            c = c[c >= np.uint32(km)].astype(np.int64)
+            buf[s, 0] = c.size
+            buf[s, gb.CAND_HEAD:gb.CAND_HEAD + min(c.size, cap)] = c[:cap]
+        return torch.from_numpy(buf)
+
+    @staticmethod
+    def candidate_counts(g):
+        return g[:, :, 0].numpy().astype(np.int64)
+
+    @staticmethod
+    def _gathered(g, counts, s):
+        return {"keys": [g[r, s, gb.CAND_HEAD:gb.CAND_HEAD + int(counts[r, s])].numpy().astype(np.uint32)
+                         for r in range(g.shape[0])]}
+
+    def gathered_histograms(self, g, counts, level, prefixes):
+        return self.histograms([self._gathered(g, counts, s) for s in range(g.shape[1])], level, prefixes)
+
+    def gathered_ties(self, g, counts, keys):
+        out = np.zeros((g.shape[0], g.shape[1]), np.int64)
+        for s in range(g.shape[1]):
+            for r, k in enumerate(self._gathered(g, counts, s)["keys"]):
+                out[r, s] = int((k == np.uint32(keys[s])).sum())
+        return out
 
     def select(self, seq, key, tie_allow):
         kept, before = [], 0
@@ -90,8 +128,16 @@ def test_score_keys_match_the_library():
     assert [tria_b200.score_key(float(v)) for v in x] == oracle_py.score_keys(x).tolist()
 
 
+PROTOCOLS = {
+    "histograms": gb.global_select,
+    "candidates": gb.global_select_candidates,
+    "candidates-overflow": lambda *a: gb.global_select_candidates(*a, cap=8),     # always falls back
+}
+
+
+@pytest.mark.parametrize("protocol", sorted(PROTOCOLS))
 @pytest.mark.parametrize("heavy_ties", [False, True])
-def test_global_select_one_rank(heavy_ties):
+def test_global_select_one_rank(heavy_ties, protocol):
     import torch
     rng = np.random.default_rng(3 + heavy_ties)
     seqs, ks = [], []
@@ -99,7 +145,7 @@ def test_global_select_one_rank(heavy_ties):
         keys = _make_seq_keys(rng, 12, 0 if s == 3 else 50, 400, heavy_ties)
         seqs.append({"keys": keys})
         ks.append([0, 17, 900, 10**6][s])
-    gb.global_select(seqs, ks, lambda t: t[None], CpuBackend(), 0)
+    PROTOCOLS[protocol](seqs, ks, lambda t: t[None], CpuBackend(), 0)
     for sq, k in zip(seqs, ks):
         exp = oracle_py.global_select(sq["keys"], k)
         assert len(sq["kept"]) == len(exp)
@@ -113,7 +159,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, q):
+def _rank_main(rank, world, port, q, protocol="histograms"):
     import torch
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -130,18 +176,19 @@ def _rank_main(rank, world, port, q):
             dist.all_gather(out, t.contiguous())
             return torch.stack(out)
 
-        gb.global_select(mine, ks, gather, CpuBackend(), rank)
+        PROTOCOLS[protocol](mine, ks, gather, CpuBackend(), rank)
         q.put((rank, [[k.tolist() for k in sq["kept"]] for sq in mine], [[k.tolist() for k in x] for x in all_seqs], ks))
     finally:
         dist.destroy_process_group()
 
 
-def test_global_select_two_gloo_ranks():
+@pytest.mark.parametrize("protocol", sorted(PROTOCOLS))
+def test_global_select_two_gloo_ranks(protocol):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q, protocol)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in procs]

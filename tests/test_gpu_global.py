@@ -2,9 +2,11 @@
 
 Three sequences with different lengths and decode positions in one q8_0
 geometry are scored on the device; the three-pass histogram threshold
-(tria_key_histogram / tria_key_count / tria_select_key) must keep exactly the
-oracle's global top-k of the same scores, and the compacted rows must be the
-kept rows byte for byte.
+(tria_key_histogram / tria_key_count / tria_select_key), and the one-exchange
+protocol over candidates (tria_key_gather), must keep exactly the oracle's
+global top-k of the same scores, and the compacted rows must be the kept
+rows byte for byte.  tria_key_gather itself must return the scores at or
+above a key, and report the full count when they do not fit.
 """
 import numpy as np
 import pytest
@@ -17,7 +19,8 @@ import workloads
 pytestmark = pytest.mark.gpu
 
 
-def test_global_budget_vs_oracle(torch_dev, tmp_path):
+@pytest.mark.parametrize("protocol", ["histograms", "candidates"])
+def test_global_budget_vs_oracle(torch_dev, tmp_path, protocol):
     import torch
     import devcache
     L, H, KV, hd, cells = 3, 32, 8, 128, 3000
@@ -40,7 +43,8 @@ def test_global_budget_vs_oracle(torch_dev, tmp_path):
                          "kept_stride": cells, "n_kept": nk})
             caches.append(c)
             ks.append(budget * L * KV)
-        gb.global_select(seqs, ks, lambda t: t[None], gb.DeviceBackend(torch_dev), 0)
+        select = gb.global_select if protocol == "histograms" else gb.global_select_candidates
+        select(seqs, ks, lambda t: t[None], gb.DeviceBackend(torch_dev), 0)
         torch.cuda.synchronize()
         for s, sq in enumerate(seqs):
             sc = sq["scores"].cpu().numpy()
@@ -64,3 +68,32 @@ def test_global_budget_vs_oracle(torch_dev, tmp_path):
         ctx.close()
     finally:
         tria_b200.free(st)
+
+
+def test_key_gather(torch_dev):
+    """The scores whose key is >= key_min, as a multiset, and the total count
+    when more than cap of them exist."""
+    import torch
+    rng = np.random.default_rng(17)
+    units, stride = 5, 4096
+    sc = rng.standard_normal((units, stride)).astype(np.float32)
+    sc[1, :40] = np.nan
+    sc[2, 100:300] = 0.5
+    n_rows = np.array([4096, 3000, 2500, 0, 1777], np.int32)
+    d_sc = torch.from_numpy(sc).to(torch_dev)
+    for key_min in (0, int(oracle_py.score_keys(np.array([0.5], np.float32))[0]), 0xFFFFFFFF):
+        live = [sc[u, :n_rows[u]] for u in range(units)]
+        allk = np.concatenate([oracle_py.score_keys(x) for x in live])
+        exp = np.sort(allk[allk >= np.uint32(key_min)])
+        for cap in (len(exp) + 8, max(1, len(exp) // 3)):
+            out = torch.zeros(cap, dtype=torch.float32, device=torch_dev)
+            cnt = torch.zeros(1, dtype=torch.int32, device=torch_dev)
+            tria_b200.key_gather(d_sc, stride, n_rows, key_min, out, cap, cnt)
+            torch.cuda.synchronize()
+            assert int(cnt.item()) == len(exp), (key_min, cap)
+            got = oracle_py.score_keys(out.cpu().numpy()[:min(cap, len(exp))])
+            if cap >= len(exp):
+                assert np.array_equal(np.sort(got), exp)
+            else:                                    # a subset of the qualifying keys
+                assert np.isin(got, exp).all() and (got >= np.uint32(key_min)).all()
+

@@ -1357,6 +1357,33 @@ extern "C" TRIA_API int tria_key_count(const float *scores, int64_t score_stride
     });
 }
 
+extern "C" TRIA_API int tria_key_gather(const float *scores, int64_t score_stride, const int32_t *n_rows,
+                                        int32_t units, uint32_t key_min, float *out, int32_t cap, int32_t *count,
+                                        void *stream) {
+    int rc = key_args_check("tria_key_gather", scores, score_stride, n_rows, units);
+    if (rc) return rc;
+    if (!count || cap < 0 || (cap > 0 && !out)) FAIL(TRIA_ERR_INVALID, "tria_key_gather: bad output");
+    CUDA_TRY(cudaMemsetAsync(count, 0, sizeof(int32_t), (cudaStream_t)stream));
+    return for_unit_chunks(units, [&](int32_t u0, int32_t nu) -> int {
+        KeyArgs *a = new (std::nothrow) KeyArgs;
+        if (!a) FAIL(TRIA_ERR_NOMEM, "host allocation failed");
+        memset(a, 0, sizeof *a);
+        a->scores = scores + (int64_t)u0 * score_stride;
+        a->score_stride = score_stride;
+        a->units = nu;
+        a->key = key_min;
+        a->n_kept = count;
+        int mx = 0;
+        for (int u = 0; u < nu; u++) { a->n_rows[u] = n_rows[u0 + u]; mx = std::max(mx, a->n_rows[u]); }
+        if (nu > 0 && mx > 0)
+            k_key_gather<<<dim3((unsigned)std::min((mx + 255) / 256, 64), (unsigned)nu), 256, 0,
+                           (cudaStream_t)stream>>>(*a, out, cap);
+        delete a;
+        CUDA_TRY(cudaGetLastError());
+        return TRIA_OK;
+    });
+}
+
 extern "C" TRIA_API int tria_select_key(const float *scores, int64_t score_stride, const int32_t *n_rows,
                                         int32_t units, uint32_t key, const int32_t *counts, int64_t tie_allow,
                                         int32_t *kept_idx, int64_t kept_stride, int32_t *n_kept, void *stream) {

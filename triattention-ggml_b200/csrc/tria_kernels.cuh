@@ -2163,6 +2163,30 @@ __global__ void __launch_bounds__(SELECT_THREADS) k_key_count(const KeyArgs a) {
     if (threadIdx.x == 0) a.counts_out[u] = c;
 }
 
+/* Scores whose key is at least a.key, from every unit, appended to out[] in
+ * no particular order: a warp takes one slot range per 32 rows with one
+ * atomic; *count gets the total, and only the first `cap` are stored.
+ * (a.kept_idx is reinterpreted as the float output, a.n_kept as the count.) */
+__global__ void __launch_bounds__(256) k_key_gather(const KeyArgs a, float *out, int32_t cap) {
+    const int u = blockIdx.y;
+    const int n = a.n_rows[u];
+    const float *sc = a.scores + (int64_t)u * a.score_stride;
+    const int lane = threadIdx.x & 31;
+    const unsigned lt = (1u << lane) - 1u;
+    for (int b = blockIdx.x * blockDim.x + (threadIdx.x & ~31); b < n; b += gridDim.x * blockDim.x) {
+        const int r = b + lane;
+        const float v = r < n ? sc[r] : 0.f;
+        const bool take = r < n && score_key(v) >= a.key;
+        const unsigned m = __ballot_sync(0xffffffffu, take);
+        if (!m) continue;
+        int base = 0;
+        if (lane == 0) base = atomicAdd(a.n_kept, __popc(m));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        const int pos = base + __popc(m & lt);
+        if (take && pos < cap) out[pos] = v;
+    }
+}
+
 __global__ void __launch_bounds__(SELECT_THREADS) k_select_key(const KeyArgs a) {
     __shared__ int s_warp[32];
     const int u = blockIdx.x, tid = threadIdx.x, bd = blockDim.x;

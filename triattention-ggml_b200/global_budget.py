@@ -18,16 +18,26 @@ agree on one threshold key per sequence through three all-gathers:
 Every rank then keeps rows with key > T_s plus its share of the rows equal
 to T_s, which makes the kept sets exactly the global top K_s.
 
+global_select_candidates reaches the same kept sets with one all-gather: each
+rank finds its own K_s-th largest key (steps 1-2 on its own rows), gathers
+the scores at or above it (tria_key_gather), and every rank runs steps 1-3 on
+the gathered candidates.  The global K_s-th key is never below a rank's own,
+so the candidates hold every kept row and every row equal to the threshold.
+If a rank has more candidates than the exchange buffer holds (many ties at
+its own threshold), every rank sees that in the gathered counts and falls
+back to global_select.
+
 The arithmetic of the device path lives in the C ABI (tria_key_histogram,
-tria_key_count, tria_select_key); this module is the host orchestration,
-written against a small backend interface so that the same code runs on the
-GPU with NCCL and, in tests, on CPU gloo ranks.
+tria_key_count, tria_select_key, tria_key_gather); this module is the host
+orchestration, written against a small backend interface so that the same
+code runs on the GPU with NCCL and, in tests, on CPU gloo ranks.
 """
 from __future__ import annotations
 
 import numpy as np
 
 NBINS = 1 << 16
+CAND_HEAD = 4        # header floats of a candidate row (count first); keeps the scores 16-byte aligned
 
 
 def boundary_bin(hist, need):
@@ -111,6 +121,50 @@ class DeviceBackend:
         tria_b200.select_key(seq["scores"], seq["stride"], seq["n_rows"], key, seq["_counts"], tie_allow,
                              seq["kept_idx"], seq["kept_stride"], seq["n_kept"], self.stream)
 
+    # ---- one exchange (global_select_candidates) ----
+
+    def rows(self, seq):
+        return int(np.asarray(seq["n_rows"], np.int64).sum())
+
+    def candidates(self, seqs, key_mins, cap):
+        """[n_seq, CAND_HEAD + cap] fp32: column 0 the candidate count, then the
+        scores whose key is >= key_mins[s] (tria_key_gather)."""
+        import torch
+        import tria_b200
+        buf = torch.zeros((len(seqs), CAND_HEAD + cap), dtype=torch.float32, device=self.device)
+        cnt = torch.zeros(len(seqs), dtype=torch.int32, device=self.device)
+        for s, (sq, k) in enumerate(zip(seqs, key_mins)):
+            tria_b200.key_gather(sq["scores"], sq["stride"], sq["n_rows"], k, buf[s, CAND_HEAD:], cap,
+                                 cnt[s:s + 1], self.stream)
+        buf[:, 0] = cnt.to(torch.float32)
+        return buf
+
+    @staticmethod
+    def candidate_counts(g):
+        """Host [world, n_seq] candidate counts of the gathered buffers."""
+        import torch
+        return g[:, :, 0].to(torch.int64).cpu().numpy()
+
+    def _gathered(self, g, counts, s):
+        """Sequence s of the gathered buffers as `world` units of candidate scores."""
+        world, n_seq, width = g.shape
+        return {"scores": g[:, s, CAND_HEAD:], "stride": n_seq * width,
+                "n_rows": np.minimum(counts[:, s], width - CAND_HEAD).astype(np.int32)}
+
+    def gathered_histograms(self, g, counts, level, prefixes):
+        return self.histograms([self._gathered(g, counts, s) for s in range(g.shape[1])], level, prefixes)
+
+    def gathered_ties(self, g, counts, keys):
+        """Host [world, n_seq]: each rank's candidates equal to keys[s]."""
+        import torch
+        import tria_b200
+        world, n_seq = g.shape[0], g.shape[1]
+        out = torch.zeros((n_seq, world), dtype=torch.int32, device=self.device)
+        for s in range(n_seq):
+            sq = self._gathered(g, counts, s)
+            tria_b200.key_count(sq["scores"], sq["stride"], sq["n_rows"], keys[s], out[s], self.stream)
+        return out.t().to(torch.int64).cpu().numpy()
+
 
 def global_select(seqs, k_total, gather, backend, rank):
     """Keep the global top k_total[s] rows of every sequence s.
@@ -160,3 +214,65 @@ def global_select(seqs, k_total, gather, backend, rank):
         backend.select(seqs[s], keys[s], allow)
         out.append((keys[s], allow))
     return out
+
+
+def global_select_candidates(seqs, k_total, gather, backend, rank, cap=None):
+    """global_select with one all-gather: same arguments and result.
+
+    cap is the candidate buffer per sequence and rank (a multiple of 4,
+    default max(k_total) + 4096); a rank with more candidates than that in
+    any sequence makes every rank fall back to global_select.
+    """
+    import torch
+    n_seq = len(seqs)
+    if cap is None:
+        cap = max([int(k) for k in k_total] + [0]) + 4096
+    cap = (int(cap) + 3) & ~3
+
+    # this rank's own K_s-th largest key: steps 1-2 on its own rows
+    rows = [backend.rows(sq) for sq in seqs]
+    kl = [min(int(k_total[s]), rows[s]) for s in range(n_seq)]
+    key_min = [0] * n_seq                                  # 0: every row is a candidate
+    part = [s for s in range(n_seq) if 0 < kl[s] < rows[s]]
+    for s in range(n_seq):
+        if kl[s] == 0:
+            key_min[s] = 0xFFFFFFFF                        # above every score key: no candidate
+    if part:
+        sub = [seqs[s] for s in part]
+        h0 = backend.histograms(sub, 0, [0] * len(part))
+        b0 = boundary_bins(h0, [kl[s] for s in part])
+        h1 = backend.histograms(sub, 1, [b for b, _ in b0])
+        for s, (b, _), (t, _) in zip(part, b0, boundary_bins(h1, [need for _, need in b0])):
+            key_min[s] = (b << 16) | t
+
+    # the one exchange
+    g = gather(backend.candidates(seqs, key_min, cap))     # [world, n_seq, CAND_HEAD + cap]
+    counts = backend.candidate_counts(g)                   # host [world, n_seq]
+    if (counts > cap).any():
+        return global_select(seqs, k_total, gather, backend, rank)
+
+    # steps 1-3 on the gathered candidates, the same on every rank
+    totals = counts.sum(0)
+    ks = [min(int(k_total[s]), int(totals[s])) for s in range(n_seq)]
+    live = [s for s in range(n_seq) if ks[s] > 0]
+    keys, needs2 = [0xFFFFFFFF] * n_seq, [0] * n_seq
+    if live:
+        gh0 = backend.gathered_histograms(g, counts, 0, [0] * n_seq)
+        bins = [0] * n_seq
+        needs = [0] * n_seq
+        for s, (b, need) in zip(live, boundary_bins(gh0[live], [ks[s] for s in live])):
+            bins[s], needs[s] = b, need
+        gh1 = backend.gathered_histograms(g, counts, 1, bins)
+        for s, (t, need2) in zip(live, boundary_bins(gh1[live], [needs[s] for s in live])):
+            keys[s] = (bins[s] << 16) | t
+            needs2[s] = need2
+    ties = backend.gathered_ties(g, counts, keys)           # host [world, n_seq]
+    out = []
+    for s in range(n_seq):
+        before = int(ties[:rank, s].sum())
+        allow = max(0, min(needs2[s] - before, int(ties[rank, s])))
+        backend.count(seqs[s], keys[s])                     # this rank's per-unit ties, for the selection
+        backend.select(seqs[s], keys[s], allow)
+        out.append((keys[s], allow))
+    return out
+

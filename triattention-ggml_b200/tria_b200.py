@@ -201,6 +201,8 @@ def lib() -> C.CDLL:
                                       C.POINTER(EvictParams), C.c_void_p]
         L.tria_ctx_set_wait_limit.argtypes = [C.c_void_p, C.c_int64]
         L.tria_ctx_set_select_split.argtypes = [C.c_void_p, C.c_int32]
+        L.tria_key_gather.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int32, C.c_uint32,
+                                      C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p]
         L.tria_checked_build.argtypes = []
         L.tria_select_noalloc.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int32,
                                           C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
@@ -302,6 +304,14 @@ def key_histogram(scores, score_stride, n_rows, level, prefix, hist, stream=None
     nr = np.ascontiguousarray(n_rows, np.int32)
     check(lib().tria_key_histogram(_ptr(scores), int(score_stride), nr.ctypes.data, int(nr.shape[0]),
                                    int(level), int(prefix), _ptr(hist), _stream(stream)))
+
+
+def key_gather(scores, score_stride, n_rows, key_min, out, cap, count, stream=None):
+    """tria_key_gather: scores of the units' rows with key >= key_min into
+    device `out` [cap]; device `count` [1] int32 gets how many there were."""
+    nr = np.ascontiguousarray(n_rows, np.int32)
+    check(lib().tria_key_gather(_ptr(scores), int(score_stride), nr.ctypes.data, int(nr.shape[0]),
+                                int(key_min), _ptr(out), int(cap), _ptr(count), _stream(stream)))
 
 
 def key_count(scores, score_stride, n_rows, key, counts, stream=None):
