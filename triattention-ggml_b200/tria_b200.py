@@ -158,7 +158,7 @@ def n_kv_per_seq(n_kept, seq_of_unit, n_seq):
 
 def build() -> str:
     """Compile the library (and the checked build) in-tree (nvcc, sm_100a)."""
-    subprocess.run(["make", "-s", "-C", HERE, "all", "checked"], check=True)
+    subprocess.run(["make", "-s", "-j4", "-C", HERE, "all", "checked"], check=True)
     return LIB_PATH
 
 
