@@ -26,6 +26,18 @@
 
 using namespace tria;
 
+/* The step's completion event.  Inside a stream capture a plain record only
+ * orders work within the capture; recorded as an external event node it is
+ * recorded again at every replay of the graph, so tria_get_n_kv waits for the
+ * replayed step. */
+static cudaError_t record_done(cudaEvent_t ev, cudaStream_t st) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(st, &cs);
+    if (e != cudaSuccess) return e;
+    return cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal)
+                                               : cudaEventRecord(ev, st);
+}
+
 /* NVTX ranges on the host timeline (a profiler shows them beside the
  * kernels; ncu --nvtx filters launches by them): a call, and the stages of an
  * eviction step.  With no tool attached a push or pop is a branch. */
@@ -1056,7 +1068,7 @@ extern "C" TRIA_API int tria_evict(tria_ctx *c, const tria_kv_view *s, const tri
     c->have_timing = c->timing;
     CUDA_TRY(cudaMemcpyAsync(c->h_pinned, c->d_status, 4, cudaMemcpyDeviceToHost, st));
     CUDA_TRY(cudaMemcpyAsync(c->h_pinned + 1, cnt, (size_t)units * 4, cudaMemcpyDeviceToHost, st));
-    CUDA_TRY(cudaEventRecord(c->ev_done, st));
+    CUDA_TRY(record_done(c->ev_done, st));
     c->last_units = (int32_t)units;
     c->have_step = true;
     return TRIA_OK;
@@ -1266,7 +1278,7 @@ extern "C" TRIA_API int tria_evict_host(tria_ctx *c, const tria_kv_view *s, cons
         CUDA_TRY(cudaMemcpyAsync(c->h_pinned, c->d_status, 4, cudaMemcpyDeviceToHost, st));
     }
     CUDA_TRY(cudaMemcpyAsync(c->h_pinned + 1, c->d_cnt_all, (size_t)units * 4, cudaMemcpyDeviceToHost, st));
-    CUDA_TRY(cudaEventRecord(c->ev_done, st));
+    CUDA_TRY(record_done(c->ev_done, st));
     c->last_units = (int32_t)units;
     c->have_step = true;
     return TRIA_OK;
