@@ -367,7 +367,7 @@ def run_ours(args):
             per_step = ctx.launches() - l0
             step_fn = lambda: ctx.evict(sv, dv, n_rows, params, stream=stream)   # noqa: E731
             graph = None
-            if not args.no_graph and world == 1:
+            if not args.no_graph:
                 graph = torch.cuda.CUDAGraph()
                 # thread-local: other threads (NCCL's watchdog) keep working during the capture
                 with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
@@ -490,7 +490,7 @@ def run_ours(args):
                    "shard": (f"layers {layer0}..{layer0 + L - 1} of {c['L']} on rank 0 (contiguous blocks)"
                              if args.scaling == "strong" and world > 1 else f"{c['L']} layers x {n_head_kv} kv heads per rank"),
                    "l2": "inputs larger than L2 (no flush)",
-                   "launch": "eager tria_evict calls" if args.no_graph or world > 1 else
+                   "launch": "eager tria_evict calls" if args.no_graph else
                              "tria_evict captured once in a CUDA graph, replayed each step"},
         "roofline": {"bound": "hbm", "kernel": "k_score_ws", "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
@@ -835,8 +835,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
     ap.add_argument("--no-graph", action="store_true",
-                    help="time eager tria_evict calls instead of replaying the step captured in a CUDA graph "
-                         "(one GPU; ranks of a multi-GPU run time eager calls)")
+                    help="time eager tria_evict calls instead of replaying the step captured in a CUDA graph")
     ap.add_argument("--global-protocol", default="histograms", choices=["histograms", "candidates"],
                     help="multiseq-q8_0-global: three all-gathers of key histograms, or one of candidates")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
