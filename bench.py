@@ -366,13 +366,19 @@ def run_ours(args):
             ctx.evict(sv, dv, n_rows, params, stream=stream)
             per_step = ctx.launches() - l0
             step_fn = lambda: ctx.evict(sv, dv, n_rows, params, stream=stream)   # noqa: E731
-            graph = None
+            graph, launch_mode = None, "eager tria_evict calls"
             if not args.no_graph:
-                graph = torch.cuda.CUDAGraph()
-                # thread-local: other threads (NCCL's watchdog) keep working during the capture
-                with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
-                    ctx.evict(sv, dv, n_rows, params, stream=stream)
-                step_fn = graph.replay
+                try:
+                    graph = torch.cuda.CUDAGraph()
+                    # thread-local: other threads (NCCL's watchdog) keep working during the capture
+                    with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
+                        ctx.evict(sv, dv, n_rows, params, stream=stream)
+                    step_fn = graph.replay
+                    launch_mode = "tria_evict captured once in a CUDA graph, replayed each step"
+                except Exception as e:                  # noqa: BLE001 - time eager calls instead
+                    graph = None
+                    launch_mode = f"eager tria_evict calls (graph capture failed: {type(e).__name__})"
+                    torch.cuda.synchronize()
                 for _ in range(max(3, args.warmup)):
                     step_fn()
                 stream.synchronize()
@@ -490,8 +496,7 @@ def run_ours(args):
                    "shard": (f"layers {layer0}..{layer0 + L - 1} of {c['L']} on rank 0 (contiguous blocks)"
                              if args.scaling == "strong" and world > 1 else f"{c['L']} layers x {n_head_kv} kv heads per rank"),
                    "l2": "inputs larger than L2 (no flush)",
-                   "launch": "eager tria_evict calls" if args.no_graph else
-                             "tria_evict captured once in a CUDA graph, replayed each step"},
+                   "launch": launch_mode},
         "roofline": {"bound": "hbm", "kernel": "k_score_ws", "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
                      "traffic": traffic, "peak_source": f"{peak_src} hbm_gbs",
