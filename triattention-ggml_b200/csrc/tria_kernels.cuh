@@ -1737,11 +1737,27 @@ __device__ __forceinline__ bool select_rows_ok(const SelectArgs &a, int n, int64
            n <= (fused ? a.raw_stride : a.score_stride);
 }
 
+/* The sum of a thread's bins [t*c, t*c + c) of a digit histogram h.  V4
+ * (1024-thread blocks, h 16-byte aligned): one 16-byte load when c == 4, which
+ * also avoids the 4-way bank conflict of four strided scalar loads. */
+template <bool V4>
+__device__ __forceinline__ int bins_sum(const int *h, int t, int c, int nb) {
+    if constexpr (V4) {
+        if (c == 4 && t * 4 + 3 < nb) {
+            const int4 v = *reinterpret_cast<const int4 *>(h + t * 4);
+            return v.x + v.y + v.z + v.w;
+        }
+    }
+    int own = 0;
+    for (int i = 0; i < c; i++) own += t * c + i < nb ? h[t * c + i] : 0;
+    return own;
+}
+
 /* Selection of unit u by the whole block: keys (in `keys`, shared or global
  * memory), radix select, ordered output.  FUSED: keys from the raw scores and
  * the (mean, std) of the unit's query heads in s_zs (shared); else from
  * a.scores.  s_hist is the block's [4096] histogram. */
-template <bool FUSED>
+template <bool FUSED, bool V4 = false>
 __device__ __forceinline__ void select_unit(const SelectArgs &a, int u, uint32_t *keys, int64_t key_cap,
                                             const float2 *s_zs, int *s_hist, int *s_warp, int *s_bc) {
     const int tid = threadIdx.x, bd = blockDim.x;
@@ -1841,8 +1857,7 @@ __device__ __forceinline__ void select_unit(const SelectArgs &a, int u, uint32_t
         }
         /* thread t owns bins [t*c, t*c + c); count of keys in bins >= its first */
         const int c = (nb + bd - 1) / bd;
-        int own = 0;
-        for (int i = 0; i < c; i++) own += tid * c + i < nb ? s_hist[tid * c + i] : 0;
+        const int own = bins_sum<V4>(s_hist, tid, c, nb);
         const int incl = block_suffix_sum(own, s_warp);
         const int above = incl - own;
         if (above < need && need <= incl) {
@@ -1869,14 +1884,14 @@ __device__ __forceinline__ void select_unit(const SelectArgs &a, int u, uint32_t
  * histogram is built in the key pass. */
 template <bool FUSED, bool SMK>
 __global__ void __launch_bounds__(SMK ? SELECT_BLOCK_SM : SELECT_BLOCK, SMK ? 1 : 2) k_select(const SelectArgs a) {
-    __shared__ int s_hist[4096];
+    __shared__ __align__(16) int s_hist[4096];
     __shared__ int s_warp[32];
     __shared__ int s_bc[2];
     __shared__ float2 s_zs[TRIA_MAX_GQA];           /* (mean, std) of the unit's query heads */
     extern __shared__ __align__(16) uint32_t s_keys[];
     const int u = blockIdx.x;
     if (FUSED && (int)threadIdx.x < a.G) s_zs[threadIdx.x] = a.ms[(int64_t)u * a.G + threadIdx.x];
-    select_unit<FUSED>(a, u, SMK ? s_keys : a.keys + (int64_t)u * a.key_stride,
+    select_unit<FUSED, SMK>(a, u, SMK ? s_keys : a.keys + (int64_t)u * a.key_stride,
                        SMK ? (int64_t)(dynamic_smem_bytes() / 4) : a.key_stride, s_zs, s_hist, s_warp, s_bc);
 }
 
@@ -1919,7 +1934,7 @@ __host__ __device__ __forceinline__ int select_cl_chunk(int n, int cl) { return 
  *    CTAs before it. */
 template <bool FUSED>
 __global__ void __launch_bounds__(SELECT_BLOCK_SM, 1) k_select_cl(const SelectArgs a) {
-    __shared__ int s_h0[4096], s_h1[1024], s_h2[1024];
+    __shared__ __align__(16) int s_h0[4096], s_h1[1024], s_h2[1024];
     __shared__ int s_gt[32], s_eq[32];
     __shared__ int s_warp[32];
     __shared__ int s_bc[2];
@@ -2020,10 +2035,7 @@ __global__ void __launch_bounds__(SELECT_BLOCK_SM, 1) k_select_cl(const SelectAr
     auto merged = [&](int *h, int nb) {
         const int c = (nb + bd - 1) / bd;
         int own = 0;
-        for (int rk = 0; rk < ncl; rk++) {
-            const int *hr = at_rank(h, rk);
-            for (int i = 0; i < c; i++) own += tid * c + i < nb ? hr[tid * c + i] : 0;
-        }
+        for (int rk = 0; rk < ncl; rk++) own += bins_sum<true>(at_rank(h, rk), tid, c, nb);
         return own;
     };
     uint32_t prefix = 0;
