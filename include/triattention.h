@@ -285,9 +285,9 @@ TRIA_API int tria_checked_build(void);
 
 /* Tuning: the most CTAs that selection may give one (layer, kv-head) unit
  * (up to 8).  0, the default, lets the library split a unit over a
- * thread-block cluster of 2 CTAs when a launch has fewer units than SMs; 1
- * keeps one block per unit.  Results are the same either way.  New; no
- * reference counterpart. */
+ * thread-block cluster of up to 4 CTAs when a launch has fewer units than
+ * SMs; 1 keeps one block per unit.  Results are the same either way.  New;
+ * no reference counterpart. */
 TRIA_API int tria_ctx_set_select_split(tria_ctx *ctx, int32_t max_ctas);
 
 /* Device-pointer form of tria_score_kv_head for one (layer, kv-head):

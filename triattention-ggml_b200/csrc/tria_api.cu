@@ -755,10 +755,11 @@ static int max_active_clusters(bool fused, int cl) {
  * memory.  1 means k_select. */
 static int select_split(const tria_ctx *c, int units, int n_max, bool fused) {
     if (c->select_split == 1 || units <= 0) return 1;
-    /* automatic: two CTAs.  Measured on B200 (32768-row units, 40 units):
-     * 44 us with one block, 36 us with two, 40 us with three or four; more
-     * CTAs spend what they save on reading each other's histograms. */
-    const int cap = c->select_split > 1 ? std::min(c->select_split, 8) : 2;
+    /* automatic: up to four CTAs.  Measured on B200 (32768-row units): 40
+     * units 42 us with one block, 34 with two, 32 with three; 32 units 30 us
+     * with four; 16 units 28 us with four and 32 with eight, where reading
+     * every other CTA's histograms costs more than the split saves. */
+    const int cap = c->select_split > 1 ? std::min(c->select_split, 8) : 4;
     for (int cl = std::min(cap, c->sm_count / units); cl >= 2; cl--) {
         if (select_cl_chunk(n_max, cl) > SELECT_SMEM_KEYS) break;    /* fewer CTAs: larger shares */
         if (units <= max_active_clusters(fused, cl)) return cl;

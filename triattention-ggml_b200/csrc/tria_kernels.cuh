@@ -1600,14 +1600,20 @@ struct SelectArgs {
     int32_t keep_req[TRIA_MAX_UNITS];
 };
 
-__device__ __forceinline__ int block_sum(int v, int *s_warp) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+__device__ __forceinline__ int warp_sum(int v) {
 #pragma unroll
     for (int m = 16; m; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    return v;
+}
+
+/* The warps' totals are folded with one shared load per lane and a warp
+ * reduction (not a loop of dependent loads); blocks of up to 32 warps. */
+__device__ __forceinline__ int block_sum(int v, int *s_warp) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum(v);
     if (lane == 0) s_warp[w] = v;
     __syncthreads();
-    int t = 0;
-    for (int i = 0; i < nw; i++) t += s_warp[i];
+    const int t = warp_sum(lane < nw ? s_warp[lane] : 0);
     __syncthreads();
     return t;
 }
@@ -1623,7 +1629,7 @@ __device__ __forceinline__ int block_suffix_sum(int v, int *s_warp) {
     }
     if (lane == 0) s_warp[w] = incl;                     /* warp total */
     __syncthreads();
-    for (int i = w + 1; i < nw; i++) incl += s_warp[i];
+    incl += warp_sum(lane > w && lane < nw ? s_warp[lane] : 0);   /* the warps after this one */
     __syncthreads();
     return incl;
 }
@@ -1670,13 +1676,9 @@ __device__ __forceinline__ int ordered_write(int n, uint32_t T, int allow, int32
     const int per_w = ordered_rows_per_warp(n);
     const int r0 = min(n, w * per_w), r1 = min(n, r0 + per_w);
     const unsigned lt = (1u << lane) - 1u;
-    int gt_before = 0, eq_before = 0, gt_blk = 0, eq_blk = 0;
-    for (int i = 0; i < nw; i++) {
-        const int g = s_gt[i], e = s_eq[i];
-        if (i < w) { gt_before += g; eq_before += e; }
-        gt_blk += g;
-        eq_blk += e;
-    }
+    const int g = lane < nw ? s_gt[lane] : 0, e = lane < nw ? s_eq[lane] : 0;   /* warp `lane`'s counts */
+    int gt_before = warp_sum(lane < w ? g : 0), eq_before = warp_sum(lane < w ? e : 0);
+    const int gt_blk = warp_sum(g), eq_blk = warp_sum(e);
     const int4 t = totals(gt_blk, eq_blk);               /* rows of the unit before this block's */
     gt_before += t.x;
     eq_before += t.y;
