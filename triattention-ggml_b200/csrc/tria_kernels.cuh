@@ -1739,6 +1739,42 @@ __device__ __forceinline__ bool select_rows_ok(const SelectArgs &a, int n, int64
            n <= (fused ? a.raw_stride : a.score_stride);
 }
 
+/* z-scores of 8 rows (rb..rb+3 and rb+4*bd..rb+4*bd+3, those below `lim`) of
+ * the unit's G query-head chains, max over the group as group_zmax
+ * (triattention.c:240-247), into x[].  PF (blocks with registers to spare):
+ * each head's two 16-byte loads are issued while the head before computes.
+ * Raw rows are 16-byte aligned and padded to a multiple of 64 floats, so a
+ * load that starts below lim stays inside the row. */
+template <bool PF>
+__device__ __forceinline__ void zmax8(const float *raw, int64_t raw_stride, const float2 *s_zs, int G, int64_t u,
+                                      int rb, int step4, int lim, float (&x)[8]) {
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    auto load = [&](int g, float4 &w0, float4 &w1) {
+        const float *xr = raw + (u * G + g) * raw_stride;
+        w0 = rb < lim ? *reinterpret_cast<const float4 *>(xr + rb) : z4;
+        w1 = rb + step4 < lim ? *reinterpret_cast<const float4 *>(xr + rb + step4) : z4;
+    };
+    float4 n0, n1;
+    if (PF) load(0, n0, n1);
+    for (int g = 0; g < G; g++) {
+        float4 v0, v1;
+        if constexpr (PF) {
+            v0 = n0;
+            v1 = n1;
+            if (g + 1 < G) load(g + 1, n0, n1);
+        } else {
+            load(g, v0, v1);
+        }
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        const float2 m = s_zs[g];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float z = __fdiv_rn(__fsub_rn(v[j], m.x), m.y);
+            if (g == 0 || z > x[j]) x[j] = z;
+        }
+    }
+}
+
 /* The sum of a thread's bins [t*c, t*c + c) of a digit histogram h.  V4
  * (1024-thread blocks, h 16-byte aligned): one 16-byte load when c == 4, which
  * also avoids the 4-way bank conflict of four strided scalar loads. */
@@ -1758,8 +1794,10 @@ __device__ __forceinline__ int bins_sum(const int *h, int t, int c, int nb) {
 /* Selection of unit u by the whole block: keys (in `keys`, shared or global
  * memory), radix select, ordered output.  FUSED: keys from the raw scores and
  * the (mean, std) of the unit's query heads in s_zs (shared); else from
- * a.scores.  s_hist is the block's [4096] histogram. */
-template <bool FUSED, bool V4 = false>
+ * a.scores.  s_hist is the block's [4096] histogram.  SMK: a 1024-thread
+ * block with its keys in shared memory and registers to spare (prefetched
+ * raw scores, 16-byte histogram reads). */
+template <bool FUSED, bool SMK = false>
 __device__ __forceinline__ void select_unit(const SelectArgs &a, int u, uint32_t *keys, int64_t key_cap,
                                             const float2 *s_zs, int *s_hist, int *s_warp, int *s_bc) {
     const int tid = threadIdx.x, bd = blockDim.x;
@@ -1781,20 +1819,7 @@ __device__ __forceinline__ void select_unit(const SelectArgs &a, int u, uint32_t
 #pragma unroll
         for (int j = 0; j < SB; j++) x[j] = 0.f;
         if constexpr (FUSED) {
-            /* z-score max over the group, as group_zmax (triattention.c:240-247) */
-            for (int g = 0; g < a.G; g++) {
-                const float *xr = a.raw + ((int64_t)u * a.G + g) * a.raw_stride;
-                const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                const float4 v0 = rb < n ? *reinterpret_cast<const float4 *>(xr + rb) : z4;
-                const float4 v1 = rb + 4 * bd < n ? *reinterpret_cast<const float4 *>(xr + rb + 4 * bd) : z4;
-                const float v[SB] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-                const float2 m = s_zs[g];
-#pragma unroll
-                for (int j = 0; j < SB; j++) {
-                    const float z = __fdiv_rn(__fsub_rn(v[j], m.x), m.y);
-                    if (g == 0 || z > x[j]) x[j] = z;
-                }
-            }
+            zmax8<SMK>(a.raw, a.raw_stride, s_zs, a.G, u, rb, 4 * bd, n, x);
         } else {
 #pragma unroll
             for (int j = 0; j < SB; j++)
@@ -1859,7 +1884,7 @@ __device__ __forceinline__ void select_unit(const SelectArgs &a, int u, uint32_t
         }
         /* thread t owns bins [t*c, t*c + c); count of keys in bins >= its first */
         const int c = (nb + bd - 1) / bd;
-        const int own = bins_sum<V4>(s_hist, tid, c, nb);
+        const int own = bins_sum<SMK>(s_hist, tid, c, nb);
         const int incl = block_suffix_sum(own, s_warp);
         const int above = incl - own;
         if (above < need && need <= incl) {
@@ -1977,20 +2002,7 @@ __global__ void __launch_bounds__(SELECT_BLOCK_SM, 1) k_select_cl(const SelectAr
 #pragma unroll
         for (int j = 0; j < SB; j++) x[j] = 0.f;
         if constexpr (FUSED) {
-            /* z-score max over the group, as group_zmax (triattention.c:240-247) */
-            for (int g = 0; g < a.G; g++) {
-                const float *xr = a.raw + ((int64_t)u * a.G + g) * a.raw_stride;
-                const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                const float4 v0 = *reinterpret_cast<const float4 *>(xr + rb);
-                const float4 v1 = rb + 4 * bd < r1 ? *reinterpret_cast<const float4 *>(xr + rb + 4 * bd) : z4;
-                const float v[SB] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-                const float2 ms = s_zs[g];
-#pragma unroll
-                for (int j = 0; j < SB; j++) {
-                    const float z = __fdiv_rn(__fsub_rn(v[j], ms.x), ms.y);
-                    if (g == 0 || z > x[j]) x[j] = z;
-                }
-            }
+            zmax8<true>(a.raw, a.raw_stride, s_zs, a.G, u, rb, 4 * bd, r1, x);
         } else {
 #pragma unroll
             for (int j = 0; j < SB; j++)
